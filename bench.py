@@ -1,0 +1,381 @@
+"""Benchmark of the sm_100a fused FP8 DeepSeek-V3 MoE layer.
+
+Default (N=1): BASELINE configs[1], the decode sweep T in {1,2,4,8,16,32,64}
+on one B200 with 32 local experts (offset 0, scaling 2.5). One step = one
+layer call at every T of the sweep; `value` = mean microseconds per call
+(device time from CUDA events around each call, the L2 flushed with a 256 MB
+write before every call, outside the events). `--workload mid|large` runs
+configs[2] / configs[3] instead.
+
+`--impl reference` times the reference algorithm on the host CPU cores (the
+numpy restatement in oracle/, because the reference is Python/PyTorch and
+cannot be compiled into oracle/_ref), one sweep point per step.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "us/call & TFLOP/s for FP8 DS-V3 MoE layer over T sweep; % of HBM/FP8 roofline"
+WORKLOADS = {
+    "decode_sweep": ((1, 2, 4, 8, 16, 32, 64), "BASELINE configs[1]: decode sweep, 32 local experts, offset 0"),
+    "mid": ((256, 1024), "BASELINE configs[2]: mid prefill, near-uniform routing"),
+    "large": ((4096, 8192, 16384), "BASELINE configs[3]: large prefill, +2.0 bias on 4 hot local experts"),
+}
+L2_FLUSH_BYTES = 256 << 20
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during timing."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.proc = None
+        self.gpu = gpu_index
+        self.path = os.path.join("/tmp", f"moe_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return None
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _dist():
+    import torch.distributed as dist
+
+    n = int(os.environ.get("WORLD_SIZE", "1"))
+    if n > 1 and not dist.is_initialized():
+        import datetime
+
+        backend = "nccl"
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    return int(os.environ.get("RANK", "0")), n
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def bench_ours(args):
+    import numpy as np
+    import torch
+
+    rank, world = _dist()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pkg = importlib.import_module("flashinfer-mlsys_b200")
+    wl = importlib.import_module("flashinfer-mlsys_b200.workloads")
+    lib = pkg.load()
+    Ts, wdesc = WORKLOADS[args.workload]
+    if args.T:
+        Ts = tuple(int(t) for t in args.T.split(","))
+    offset = 0
+    w = wl.make_weights(32, offset, dev)
+    acts = {T: wl.config_activations(T, offset) for T in Ts}
+    acts_gpu = {T: acts[T].to(dev) for T in Ts}
+    outs = {T: torch.empty((T, 7168), dtype=torch.bfloat16, device=dev) for T in Ts}
+    counts = {T: torch.zeros((32,), dtype=torch.int32, device=dev) for T in Ts}
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def call(T, cnt=None):
+        a = acts_gpu[T]
+        pkg.kernel_ex(a.logits, a.bias, a.hidden, a.hidden_scale, w.w13, w.s13, w.w2, w.s2, offset, 2.5, outs[T],
+                      None, None, cnt)
+
+    # routing statistics for the algorithmic FLOP/byte counts
+    stats = {}
+    for T in Ts:
+        call(T, counts[T])
+    torch.cuda.synchronize()
+    for T in Ts:
+        c = counts[T].cpu().numpy()
+        stats[T] = {"n_assign": int(c.sum()), "e_touched": int((c > 0).sum())}
+
+    for _ in range(args.warmup):
+        for T in Ts:
+            flush.zero_()
+            call(T)
+    torch.cuda.synchronize()
+
+    ev = {T: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)] for T in Ts}
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for s in range(args.steps):
+            for T in Ts:
+                flush.zero_()
+                ev[T][s][0].record(stream)
+                call(T)
+                ev[T][s][1].record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+    per_T_ms = {T: statistics.mean(a.elapsed_time(b) for a, b in ev[T]) for T in Ts}
+    if pkg.device_status() != 0:
+        raise RuntimeError("device-side wait timed out during the benchmark")
+    step_ms = sum(per_T_ms.values())
+    if world > 1:
+        t = torch.tensor([step_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        step_ms = float(t.item())
+
+    # per-kernel device times (CUDA events recorded by the library on this stream)
+    lib.moe_fp8_ds_profile_enable(1)
+    kern = {T: np.zeros(5) for T in Ts}
+    buf = (ctypes.c_float * 5)()
+    for s in range(args.steps):
+        for T in Ts:
+            flush.zero_()
+            call(T)
+            n = lib.moe_fp8_ds_profile_last(buf, 5)
+            kern[T] += np.array(buf[:5])
+    lib.moe_fp8_ds_profile_enable(0)
+    for T in Ts:
+        kern[T] /= args.steps
+
+    # end to end through the public API with host buffers (pinned), H2D of the
+    # call's inputs and D2H of its output inside the events
+    host_in = {T: [acts[T].logits.pin_memory(), acts[T].bias.pin_memory(),
+                   acts[T].hidden.view(torch.uint8).pin_memory(), acts[T].hidden_scale.pin_memory()] for T in Ts}
+    host_out = {T: torch.empty((T, 7168), dtype=torch.bfloat16).pin_memory() for T in Ts}
+    e2e_ev = {T: [] for T in Ts}
+    for s in range(args.warmup + args.steps):
+        for T in Ts:
+            a = acts_gpu[T]
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            a.logits.copy_(host_in[T][0], non_blocking=True)
+            a.bias.copy_(host_in[T][1], non_blocking=True)
+            a.hidden.view(torch.uint8).copy_(host_in[T][2], non_blocking=True)
+            a.hidden_scale.copy_(host_in[T][3], non_blocking=True)
+            call(T)
+            host_out[T].copy_(outs[T], non_blocking=True)
+            e1.record(stream)
+            if s >= args.warmup:
+                e2e_ev[T].append((e0, e1))
+    torch.cuda.synchronize()
+    e2e_ms = {T: statistics.mean(a.elapsed_time(b) for a, b in e2e_ev[T]) for T in Ts}
+    h2d = sum(int(sum(x.numel() * x.element_size() for x in host_in[T])) for T in Ts)
+    d2h = sum(T * 7168 * 2 for T in Ts)
+
+    hbm_peak, bf16_peak, peak_src = _peaks()
+    fp8_peak = 2 * bf16_peak
+    sweep = {}
+    tot_flops = tot_bytes = 0
+    g1_bytes = g1_ms = 0.0
+    for T in Ts:
+        st = stats[T]
+        flops = wl.moe_flops(st["n_assign"])
+        byts = wl.moe_bytes(T, st["e_touched"])
+        ms = per_T_ms[T]
+        t_roof_ms = max(byts / (hbm_peak * 1e9), flops / (fp8_peak * 1e12)) * 1e3
+        sweep[str(T)] = {
+            "us": round(ms * 1e3, 2), "e2e_us": round(e2e_ms[T] * 1e3, 2), **st,
+            "tflops": round(flops / (ms * 1e-3) / 1e12, 3), "gbs": round(byts / (ms * 1e-3) / 1e9, 1),
+            "roofline_frac": round(t_roof_ms / ms, 4),
+            "kernel_us": {k: round(v * 1e3, 2) for k, v in zip(
+                ["route", "permute", "gemm1", "gemm2", "finalize"], kern[T])},
+        }
+        tot_flops += flops
+        tot_bytes += byts
+        # GEMM1 algorithmic bytes: touched W13 + scales, permuted rows in, intermediate out
+        g1_bytes += st["e_touched"] * (4096 * 7168 + 32 * 56 * 4) + st["n_assign"] * (7168 + 56 * 4 + 4096 + 64)
+        g1_ms += kern[T][2]
+    tot_ms = sum(per_T_ms.values())
+    n_calls = len(Ts)
+    value = tot_ms * 1e3 / n_calls
+    achieved = g1_bytes / (g1_ms * 1e-3) / 1e9 if g1_ms > 0 else 0.0
+    clocks = clk.summary()
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "us/call", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 (tcgen05 kind::f8f6f4)",
+        "data": "synthetic, seeded (BASELINE value distributions; contest dataset unavailable)",
+        "config": {"workload": f"{args.workload}: {wdesc}", "T": list(Ts), "num_local_experts": 32,
+                   "local_expert_offset": offset, "routed_scaling_factor": 2.5,
+                   "l2": "256 MB L2 flush before every call, outside the timed events",
+                   "parallelism": "ep1" if world == 1 else f"replicas{world}"},
+        "tflops": round(tot_flops / (tot_ms * 1e-3) / 1e12, 3),
+        "hbm_gbs_algorithmic": round(tot_bytes / (tot_ms * 1e-3) / 1e9, 1),
+        "sweep": sweep,
+        "roofline": {"bound": "hbm", "kernel": "moe_gemm_kernel<1> (GEMM1 + SwiGLU)", "achieved": round(achieved, 1),
+                     "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                     "peak_source": peak_src, "traffic": _ncu_traffic()},
+        "e2e": {"value": round(sum(e2e_ms.values()) * 1e3 / n_calls, 3), "unit": "us/call",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": 5 * n_calls * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(Ts, acts, w)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def _ncu_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p)).get("gemm1_dram_bytes_per_launch")
+        except (OSError, ValueError):
+            return None
+    return None
+
+
+# ---------------------------------------------------------------------------
+# CPU arms (oracle = numpy restatement of reference moe/ref_moe.py)
+# ---------------------------------------------------------------------------
+def _oracle_call(O, acts, get_expert, offset=0):
+    return O.moe_forward(acts.logits.numpy(), O.as_f32(acts.bias), O.as_u8(acts.hidden),
+                         acts.hidden_scale.numpy(), get_expert, offset, 2.5, 32)
+
+
+def cpu_baseline(Ts, acts, w):
+    O = importlib.import_module("oracle.moe_oracle")
+    sample = [T for T in Ts if T <= 8] or [min(Ts)]
+    cache = {}
+
+    def get_expert(le):
+        if le not in cache:
+            cache[le] = w.expert_cpu(le)
+        return cache[le]
+
+    for T in sample:  # fetch the touched experts to host memory first (not timed)
+        r = O.route(acts[T].logits.numpy(), O.as_f32(acts[T].bias), 2.5)
+        for le in set(int(x) for x in r["topk_idx"].ravel() if 0 <= x < 32):
+            get_expert(le)
+    times = []
+    for T in sample:
+        t0 = time.perf_counter()
+        _oracle_call(O, acts[T], get_expert)
+        times.append(time.perf_counter() - t0)
+    return {"value": round(statistics.mean(times) * 1e6, 1), "unit": "us/call", "cores": os.cpu_count(),
+            "kind": "port", "sample": f"one oracle call at each T in {sample} (numpy, BLAS on all cores)"}
+
+
+def bench_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    O = importlib.import_module("oracle.moe_oracle")
+    wl = importlib.import_module("flashinfer-mlsys_b200.workloads")
+    Ts, wdesc = WORKLOADS[args.workload]
+    if args.T:
+        Ts = tuple(int(t) for t in args.T.split(","))
+    cache = {}
+
+    def get_expert(le):
+        if le not in cache:
+            q13, s13, q2, s2 = wl.expert_weights(le, "cpu", 0)
+            cache[le] = (q13, s13, q2, s2)
+        return cache[le]
+
+    acts = {T: wl.config_activations(T) for T in Ts}
+    seq = [Ts[i % len(Ts)] for i in range(args.warmup + args.steps)]
+    # weights generation is setup, not the reference's work
+    for T in set(seq):
+        r = O.route(acts[T].logits.numpy(), O.as_f32(acts[T].bias), 2.5)
+        for le in set(int(x) for x in r["topk_idx"].ravel() if 0 <= x < 32):
+            get_expert(le)
+    times = []
+    for i, T in enumerate(seq):
+        t0 = time.perf_counter()
+        _oracle_call(O, acts[T], get_expert)
+        if i >= args.warmup:
+            times.append((T, time.perf_counter() - t0))
+    us = statistics.mean(t for _, t in times) * 1e6
+    line = {
+        "metric": METRIC, "value": round(us, 1), "unit": "us/call", "impl": "reference", "n_gpus": 0,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 3), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (dequantised)", "data": "synthetic, seeded",
+        "config": {"workload": f"{args.workload}: {wdesc}", "T": list(Ts), "num_local_experts": 32,
+                   "local_expert_offset": 0, "routed_scaling_factor": 2.5},
+        "cpu_baseline": {"value": round(us, 1), "unit": "us/call", "cores": os.cpu_count(), "kind": "port",
+                         "sample": "one call per step, T cycling through the sweep"},
+        "e2e": {"value": round(us, 1), "unit": "us/call", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode_sweep")
+    ap.add_argument("--T", default="", help="comma-separated token counts overriding the workload's sweep")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        bench_reference(args)
+    else:
+        bench_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,193 @@
+"""Python drop-in for the reference's destination-passing MoE entry point.
+
+``kernel(...)`` has the 11 parameters, order and meaning of
+solution/cuda/binding.py:149-161 and solution/cuda/kernel.cu:134-146
+(definition: reference moe/ref_moe.json:57-145): it writes the bf16 MoE
+output of one expert-parallel rank into the caller's ``output`` tensor.
+
+Everything runs in the sm_100a library ``libmoe_fp8_ds.so`` on the caller's
+current CUDA stream; this module only checks arguments and passes pointers.
+There is no PyTorch or CPU fallback: a missing library or a failing call
+raises.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+HIDDEN_SIZE = 7168
+INTERMEDIATE_SIZE = 2048
+NUM_EXPERTS = 256
+NUM_LOCAL_EXPERTS = 32
+BLOCK_Q = 128
+TOP_K = 8
+N_GROUP = 8
+TOPK_GROUP = 4
+
+_E4M3 = torch.float8_e4m3fn
+
+
+def _need(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def _tensor(t: torch.Tensor, name: str, dtype: torch.dtype, shape: tuple) -> None:
+    _need(isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor")
+    _need(t.is_cuda, f"{name} must be a CUDA tensor")
+    _need(t.dtype == dtype, f"{name} must be {dtype}, got {t.dtype}")
+    _need(tuple(t.shape) == tuple(shape), f"{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
+    _need(t.is_contiguous(), f"{name} must be contiguous")
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _check_weights(w1, s1, w2, s2, e_local):
+    _tensor(w1, "gemm1_weights", _E4M3, (e_local, 2 * INTERMEDIATE_SIZE, HIDDEN_SIZE))
+    _tensor(s1, "gemm1_weights_scale", torch.float32, (e_local, 2 * INTERMEDIATE_SIZE // BLOCK_Q, HIDDEN_SIZE // BLOCK_Q))
+    _tensor(w2, "gemm2_weights", _E4M3, (e_local, HIDDEN_SIZE, INTERMEDIATE_SIZE))
+    _tensor(s2, "gemm2_weights_scale", torch.float32, (e_local, HIDDEN_SIZE // BLOCK_Q, INTERMEDIATE_SIZE // BLOCK_Q))
+
+
+def kernel_ex(
+    routing_logits: torch.Tensor,
+    routing_bias: torch.Tensor,
+    hidden_states: torch.Tensor,
+    hidden_states_scale: torch.Tensor,
+    gemm1_weights: torch.Tensor,
+    gemm1_weights_scale: torch.Tensor,
+    gemm2_weights: torch.Tensor,
+    gemm2_weights_scale: torch.Tensor,
+    local_expert_offset: int,
+    routed_scaling_factor: float,
+    output: torch.Tensor,
+    topk_ids: torch.Tensor | None = None,
+    topk_weights: torch.Tensor | None = None,
+    expert_counts: torch.Tensor | None = None,
+) -> None:
+    """``kernel`` plus optional device outputs of this call's routing decision
+    (int32 [T, 8] ids, f32 [T, 8] weights, int32 [E_local] per-expert counts)."""
+    _need(routing_logits.dim() == 2, "routing_logits must be 2-D [seq_len, 256]")
+    T = routing_logits.shape[0]
+    e_local = gemm1_weights.shape[0]
+    _tensor(routing_logits, "routing_logits", torch.float32, (T, NUM_EXPERTS))
+    _tensor(routing_bias, "routing_bias", torch.bfloat16, (NUM_EXPERTS,))
+    _tensor(hidden_states, "hidden_states", _E4M3, (T, HIDDEN_SIZE))
+    _tensor(hidden_states_scale, "hidden_states_scale", torch.float32, (HIDDEN_SIZE // BLOCK_Q, T))
+    _check_weights(gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, e_local)
+    _tensor(output, "output", torch.bfloat16, (T, HIDDEN_SIZE))
+    if topk_ids is not None:
+        _tensor(topk_ids, "topk_ids", torch.int32, (T, TOP_K))
+    if topk_weights is not None:
+        _tensor(topk_weights, "topk_weights", torch.float32, (T, TOP_K))
+    if expert_counts is not None:
+        _tensor(expert_counts, "expert_counts", torch.int32, (e_local,))
+    dev = hidden_states.device
+    for t in (routing_logits, routing_bias, hidden_states_scale, gemm1_weights, gemm2_weights, output):
+        _need(t.device == dev, "all tensors must be on the same device")
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.moe_fp8_ds_kernel_ex(
+            routing_logits.data_ptr(), routing_bias.data_ptr(), hidden_states.data_ptr(),
+            hidden_states_scale.data_ptr(), gemm1_weights.data_ptr(), gemm1_weights_scale.data_ptr(),
+            gemm2_weights.data_ptr(), gemm2_weights_scale.data_ptr(), int(local_expert_offset),
+            float(routed_scaling_factor), output.data_ptr(), T, e_local,
+            _ptr(topk_ids), _ptr(topk_weights), _ptr(expert_counts), _stream(dev))
+    _lib.check(rc, "moe_fp8_ds_kernel_ex")
+
+
+@torch.no_grad()
+def kernel(
+    routing_logits: torch.Tensor,
+    routing_bias: torch.Tensor,
+    hidden_states: torch.Tensor,
+    hidden_states_scale: torch.Tensor,
+    gemm1_weights: torch.Tensor,
+    gemm1_weights_scale: torch.Tensor,
+    gemm2_weights: torch.Tensor,
+    gemm2_weights_scale: torch.Tensor,
+    local_expert_offset: int,
+    routed_scaling_factor: float,
+    output: torch.Tensor,
+) -> None:
+    """DPS MoE layer: routing, per-expert GEMM1 -> SwiGLU -> GEMM2 and the
+    weighted combine, written to ``output`` (bf16 [seq_len, 7168])."""
+    kernel_ex(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+              gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+              routed_scaling_factor, output)
+
+
+@torch.no_grad()
+def route(
+    routing_logits: torch.Tensor,
+    routing_bias: torch.Tensor,
+    local_expert_offset: int = 0,
+    num_local_experts: int = NUM_LOCAL_EXPERTS,
+    routed_scaling_factor: float = 2.5,
+):
+    """DeepSeek-V3 no-aux routing only. Returns (ids int32 [T,8], weights f32
+    [T,8], local per-expert counts int32 [num_local_experts])."""
+    _need(routing_logits.dim() == 2, "routing_logits must be 2-D [seq_len, 256]")
+    T = routing_logits.shape[0]
+    _tensor(routing_logits, "routing_logits", torch.float32, (T, NUM_EXPERTS))
+    _tensor(routing_bias, "routing_bias", torch.bfloat16, (NUM_EXPERTS,))
+    dev = routing_logits.device
+    ids = torch.empty((T, TOP_K), dtype=torch.int32, device=dev)
+    w = torch.empty((T, TOP_K), dtype=torch.float32, device=dev)
+    counts = torch.zeros((num_local_experts,), dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.moe_fp8_ds_route(routing_logits.data_ptr(), routing_bias.data_ptr(), T, int(local_expert_offset),
+                                  int(num_local_experts), float(routed_scaling_factor), ids.data_ptr(),
+                                  w.data_ptr(), counts.data_ptr(), _stream(dev))
+    _lib.check(rc, "moe_fp8_ds_route")
+    return ids, w, counts
+
+
+@torch.no_grad()
+def experts(
+    hidden_states: torch.Tensor,
+    hidden_states_scale: torch.Tensor,
+    topk_ids: torch.Tensor,
+    topk_weights: torch.Tensor,
+    gemm1_weights: torch.Tensor,
+    gemm1_weights_scale: torch.Tensor,
+    gemm2_weights: torch.Tensor,
+    gemm2_weights_scale: torch.Tensor,
+    local_expert_offset: int,
+    output: torch.Tensor,
+) -> None:
+    """Expert computation of pre-routed rows: output[r] = sum over the row's
+    local experts of weight * expert(row). ``output`` is f32 or bf16
+    [num_rows, 7168]."""
+    R = hidden_states.shape[0]
+    e_local = gemm1_weights.shape[0]
+    _tensor(hidden_states, "hidden_states", _E4M3, (R, HIDDEN_SIZE))
+    _tensor(hidden_states_scale, "hidden_states_scale", torch.float32, (HIDDEN_SIZE // BLOCK_Q, R))
+    _tensor(topk_ids, "topk_ids", torch.int32, (R, TOP_K))
+    _tensor(topk_weights, "topk_weights", torch.float32, (R, TOP_K))
+    _check_weights(gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, e_local)
+    _need(output.dtype in (torch.float32, torch.bfloat16), "output must be float32 or bfloat16")
+    _tensor(output, "output", output.dtype, (R, HIDDEN_SIZE))
+    dev = hidden_states.device
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.moe_fp8_ds_experts(
+            hidden_states.data_ptr(), hidden_states_scale.data_ptr(), topk_ids.data_ptr(), topk_weights.data_ptr(),
+            gemm1_weights.data_ptr(), gemm1_weights_scale.data_ptr(), gemm2_weights.data_ptr(),
+            gemm2_weights_scale.data_ptr(), int(local_expert_offset), R, e_local, output.data_ptr(),
+            1 if output.dtype == torch.float32 else 0, _stream(dev))
+    _lib.check(rc, "moe_fp8_ds_experts")
+
+
+def device_status(stream=None) -> int:
+    """Synchronise and return the library's device status (0 = ok)."""
+    s = torch.cuda.current_stream().cuda_stream if stream is None else stream
+    return _lib.load().moe_fp8_ds_device_status(s)

@@ -1,0 +1,344 @@
+// moe_api.cu — the C ABI (include/moe_fp8_ds.h): argument checks, cached
+// device workspace, TMA tensor maps and the launch sequence
+//   route+plan -> permute -> GEMM1(+SwiGLU+requant) -> GEMM2(+combine) -> finalize
+// on the caller's stream, with no host synchronisation.
+#include <mutex>
+#include <unordered_map>
+
+#include "../../include/moe_fp8_ds.h"
+#include "moe_kernels.h"
+
+using namespace moe;
+
+namespace {
+
+std::mutex g_mu;
+std::unordered_map<int, Workspace> g_ws;  // per device
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2D byte matrix [rows][cols] (row stride = cols bytes), 128x128 box,
+// 128-byte swizzle (matches the UMMA K-major SWIZZLE_128B operand layout).
+bool make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols};
+  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int64_t rows_cap_for(int64_t T, int e_local) {
+  const int64_t per_tok = e_local < kTopK ? e_local : kTopK;
+  return ((T * per_tok + kTileM - 1) / kTileM) * kTileM + (int64_t)e_local * kTileM;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Computes the layout; when `base` is non-null also assigns the pointers.
+// `zero_bytes` receives the length of the prefix that must start zeroed
+// (self-resetting counters, the combine accumulator, split-K scratch).
+size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_bytes) {
+  const int64_t rows = rows_cap_for(T, e_local);
+  const int ctas = route_ctas_for(static_cast<int>(T));
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off += align256(bytes);
+    return base ? base + o : nullptr;
+  };
+  const size_t Tz = static_cast<size_t>(T > 0 ? T : 1);
+  w.expert_fill = reinterpret_cast<int32_t*>(take((size_t)kExperts * 4));
+  w.done_ctas = reinterpret_cast<uint32_t*>(take(4));
+  w.status = reinterpret_cast<unsigned*>(take(4));
+  w.tile_sem = reinterpret_cast<int32_t*>(take((size_t)kMaxSplitMTiles * kNT1 * 4));
+  w.accum = reinterpret_cast<float*>(take(Tz * kHidden * 4));
+  w.g_part = reinterpret_cast<float*>(take((size_t)kMaxSplitMTiles * kTileM * kGemm1N * 4));
+  if (zero_bytes) *zero_bytes = off;
+  w.plan = reinterpret_cast<Plan*>(take(sizeof(Plan)));
+  w.topk_ids = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
+  w.topk_w = reinterpret_cast<float*>(take(Tz * kTopK * 4));
+  w.topk_rank = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
+  w.cta_off = reinterpret_cast<int32_t*>(take((size_t)(ctas > 256 ? ctas : 256) * e_local * 4));
+  w.a1 = take((size_t)rows * kHidden);
+  w.a1_scale = reinterpret_cast<float*>(take((size_t)rows * kHiddenBlocks * 4));
+  w.row_token = reinterpret_cast<int32_t*>(take((size_t)rows * 4));
+  w.row_weight = reinterpret_cast<float*>(take((size_t)rows * 4));
+  w.inter = take((size_t)rows * kInterCols);
+  w.inter_scale = reinterpret_cast<float*>(take((size_t)rows * kInterBlocks * 4));
+  w.rows_cap = rows;
+  w.t_cap = T;
+  w.e_local = e_local;
+  w.route_ctas_cap = ctas;
+  return off;
+}
+
+int get_workspace(int64_t T, int e_local, Workspace** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MOE_ERR_CUDA;
+  Workspace& w = g_ws[dev];
+  if (w.base && w.t_cap >= T && w.e_local == e_local) {
+    *out = &w;
+    return MOE_OK;
+  }
+  int64_t t_new = T;
+  if (w.base && w.e_local == e_local && w.t_cap > t_new) t_new = w.t_cap;
+  if (w.base) {
+    cudaDeviceSynchronize();
+    cudaFree(w.base);
+    w = Workspace{};
+  }
+  Workspace nw;
+  size_t zero_bytes = 0;
+  const size_t bytes = layout(nw, t_new, e_local, nullptr, &zero_bytes);
+  void* base = nullptr;
+  if (cudaMalloc(&base, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return MOE_ERR_WORKSPACE;
+  }
+  if (cudaMemset(base, 0, zero_bytes) != cudaSuccess) {
+    cudaFree(base);
+    return MOE_ERR_CUDA;
+  }
+  layout(nw, t_new, e_local, static_cast<uint8_t*>(base), nullptr);
+  nw.base = base;
+  nw.bytes = bytes;
+  w = nw;
+  *out = &w;
+  return MOE_OK;
+}
+
+int check_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MOE_ERR_NO_DEVICE;
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return MOE_ERR_NO_DEVICE;
+  return major == 10 ? MOE_OK : MOE_ERR_NO_DEVICE;
+}
+
+// Optional per-kernel CUDA events (moe_fp8_ds_profile_enable).
+constexpr int kProfKernels = 5;
+bool g_prof_on = false;
+bool g_prof_valid = false;
+cudaEvent_t g_prof_ev[kProfKernels + 1] = {};
+
+inline void prof_mark(int i, cudaStream_t s) {
+  if (g_prof_on) cudaEventRecord(g_prof_ev[i], s);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool valid_e_local(int64_t e) { return e == 32 || e == 64 || e == 128 || e == 256; }
+
+// The shared expert pipeline: plan (from logits or from given ids), permute,
+// both GEMMs and the finalize cast.
+int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids, const float* given_w,
+                 const void* hidden, const float* hidden_scale, const void* w1, const float* s1, const void* w2,
+                 const float* s2, int64_t offset, double scale, void* out, int out_fp32, int64_t T, int64_t E_l,
+                 int32_t* user_ids, float* user_w, int32_t* user_counts, void* stream, bool route_only) {
+  if (T < 0 || T > (int64_t(1) << 24) || !valid_e_local(E_l)) return MOE_ERR_INVALID_ARG;
+  if (offset < -(int64_t(1) << 30) || offset > (int64_t(1) << 30)) return MOE_ERR_INVALID_ARG;
+  if (logits) {
+    if (!bias) return MOE_ERR_INVALID_ARG;
+    if (!aligned16(logits) || !aligned16(bias)) return MOE_ERR_ALIGNMENT;
+  } else if (!given_ids || !given_w) {
+    return MOE_ERR_INVALID_ARG;
+  }
+  if (!route_only) {
+    if (!hidden || !hidden_scale || !w1 || !s1 || !w2 || !s2 || !out) return MOE_ERR_INVALID_ARG;
+    if (!aligned16(hidden) || !aligned16(w1) || !aligned16(w2) || !aligned16(out)) return MOE_ERR_ALIGNMENT;
+  }
+  int rc = check_device();
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (T == 0) return MOE_OK;
+
+  std::lock_guard<std::mutex> lk(g_mu);
+  Workspace* ws = nullptr;
+  rc = get_workspace(T, static_cast<int>(E_l), &ws);
+  if (rc) return rc;
+
+  RouteArgs ra{};
+  ra.logits = logits;
+  ra.bias = static_cast<const uint16_t*>(bias);
+  ra.given_ids = given_ids;
+  ra.given_w = given_w;
+  ra.T = static_cast<int>(T);
+  ra.offset = static_cast<int>(offset);
+  ra.e_local = static_cast<int>(E_l);
+  ra.scale = static_cast<float>(scale);
+  ra.tokens_per_cta = tokens_per_cta_for(static_cast<int>(T));
+  ra.user_ids = user_ids;
+  ra.user_w = user_w;
+  ra.user_counts = user_counts;
+  if (!route_only) prof_mark(0, s);
+  if (launch_route(*ws, ra, s) != cudaSuccess) return MOE_ERR_CUDA;
+  if (route_only) return MOE_OK;
+
+  CUtensorMap ma1, mw1, ma2, mw2;
+  if (!make_map(&ma1, ws->a1, kHidden, ws->rows_cap) ||
+      !make_map(&mw1, w1, kHidden, static_cast<uint64_t>(E_l) * kGemm1N) ||
+      !make_map(&ma2, ws->inter, kInterCols, ws->rows_cap) ||
+      !make_map(&mw2, w2, kInter, static_cast<uint64_t>(E_l) * kHidden))
+    return MOE_ERR_CUDA;
+
+  PermuteArgs pa{};
+  pa.hidden = static_cast<const uint8_t*>(hidden);
+  pa.hidden_scale = hidden_scale;
+  pa.T = static_cast<int>(T);
+  pa.offset = static_cast<int>(offset);
+  pa.tokens_per_cta = ra.tokens_per_cta;
+  prof_mark(1, s);
+  if (launch_permute(*ws, pa, s) != cudaSuccess) return MOE_ERR_CUDA;
+  prof_mark(2, s);
+  if (launch_gemm1(*ws, ma1, mw1, s1, s) != cudaSuccess) return MOE_ERR_CUDA;
+  prof_mark(3, s);
+  if (launch_gemm2(*ws, ma2, mw2, s2, s) != cudaSuccess) return MOE_ERR_CUDA;
+  prof_mark(4, s);
+  if (launch_finalize(*ws, static_cast<int>(T), out, out_fp32, s) != cudaSuccess) return MOE_ERR_CUDA;
+  prof_mark(5, s);
+  g_prof_valid = g_prof_on;
+  return MOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_fp8_ds_kernel_ex(const float* routing_logits, const void* routing_bias, const void* hidden_states,
+                         const float* hidden_states_scale, const void* gemm1_weights,
+                         const float* gemm1_weights_scale, const void* gemm2_weights,
+                         const float* gemm2_weights_scale, int64_t local_expert_offset,
+                         double routed_scaling_factor, void* output, int64_t seq_len, int64_t num_local_experts,
+                         int32_t* topk_ids_out, float* topk_weights_out, int32_t* expert_counts_out,
+                         void* stream) {
+  if (!routing_logits) return MOE_ERR_INVALID_ARG;
+  return run_pipeline(routing_logits, routing_bias, nullptr, nullptr, hidden_states, hidden_states_scale,
+                      gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+                      routed_scaling_factor, output, 0, seq_len, num_local_experts, topk_ids_out, topk_weights_out,
+                      expert_counts_out, stream, false);
+}
+
+int moe_fp8_ds_kernel(const float* routing_logits, const void* routing_bias, const void* hidden_states,
+                      const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
+                      const void* gemm2_weights, const float* gemm2_weights_scale, int64_t local_expert_offset,
+                      double routed_scaling_factor, void* output, int64_t seq_len, int64_t num_local_experts,
+                      void* stream) {
+  return moe_fp8_ds_kernel_ex(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                              gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+                              routed_scaling_factor, output, seq_len, num_local_experts, nullptr, nullptr, nullptr,
+                              stream);
+}
+
+int moe_fp8_ds_route(const float* routing_logits, const void* routing_bias, int64_t seq_len,
+                     int64_t local_expert_offset, int64_t num_local_experts, double routed_scaling_factor,
+                     int32_t* topk_ids_out, float* topk_weights_out, int32_t* expert_counts_out, void* stream) {
+  if (!routing_logits || !topk_ids_out || !topk_weights_out) return MOE_ERR_INVALID_ARG;
+  return run_pipeline(routing_logits, routing_bias, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                      nullptr, local_expert_offset, routed_scaling_factor, nullptr, 0, seq_len, num_local_experts,
+                      topk_ids_out, topk_weights_out, expert_counts_out, stream, true);
+}
+
+int moe_fp8_ds_experts(const void* hidden_states, const float* hidden_states_scale, const int32_t* topk_ids,
+                       const float* topk_weights, const void* gemm1_weights, const float* gemm1_weights_scale,
+                       const void* gemm2_weights, const float* gemm2_weights_scale, int64_t local_expert_offset,
+                       int64_t num_rows, int64_t num_local_experts, void* output, int output_fp32, void* stream) {
+  if (!topk_ids || !topk_weights) return MOE_ERR_INVALID_ARG;
+  return run_pipeline(nullptr, nullptr, topk_ids, topk_weights, hidden_states, hidden_states_scale, gemm1_weights,
+                      gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset, 1.0, output,
+                      output_fp32 ? 1 : 0, num_rows, num_local_experts, nullptr, nullptr, nullptr, stream, false);
+}
+
+const char* moe_fp8_ds_status_string(int status) {
+  switch (status) {
+    case MOE_OK: return "ok";
+    case MOE_ERR_INVALID_ARG: return "invalid argument (size, null pointer or unsupported value)";
+    case MOE_ERR_ALIGNMENT: return "tensor base address is not 16-byte aligned";
+    case MOE_ERR_CUDA: return "CUDA runtime/driver call failed";
+    case MOE_ERR_NO_DEVICE: return "no sm_100 (B200) device is current";
+    case MOE_ERR_WORKSPACE: return "device workspace allocation failed";
+    case MOE_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+int moe_fp8_ds_device_status(void* stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(s) != cudaSuccess) return MOE_ERR_CUDA;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MOE_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_ws.find(dev);
+  if (it == g_ws.end() || !it->second.base) return MOE_OK;
+  unsigned v = 0;
+  if (cudaMemcpy(&v, it->second.status, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return MOE_ERR_CUDA;
+  if (v) {
+    cudaMemset(it->second.status, 0, 4);
+    return MOE_ERR_DEVICE_TIMEOUT;
+  }
+  return MOE_OK;
+}
+
+size_t moe_fp8_ds_workspace_bytes(int64_t seq_len, int64_t num_local_experts) {
+  if (seq_len < 0 || !valid_e_local(num_local_experts)) return 0;
+  Workspace w;
+  return layout(w, seq_len, static_cast<int>(num_local_experts), nullptr, nullptr);
+}
+
+int moe_fp8_ds_release_workspace(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MOE_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_ws.find(dev);
+  if (it != g_ws.end() && it->second.base) {
+    cudaDeviceSynchronize();
+    cudaFree(it->second.base);
+    g_ws.erase(it);
+  }
+  return MOE_OK;
+}
+
+int moe_fp8_ds_profile_enable(int on) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (on && !g_prof_ev[0]) {
+    for (int i = 0; i <= kProfKernels; ++i)
+      if (cudaEventCreate(&g_prof_ev[i]) != cudaSuccess) return MOE_ERR_CUDA;
+  }
+  g_prof_on = on != 0;
+  g_prof_valid = false;
+  return MOE_OK;
+}
+
+int moe_fp8_ds_profile_last(float* ms_out, int n) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!ms_out || n <= 0) return -MOE_ERR_INVALID_ARG;
+  if (!g_prof_valid) return 0;
+  if (cudaEventSynchronize(g_prof_ev[kProfKernels]) != cudaSuccess) return -MOE_ERR_CUDA;
+  int k = n < kProfKernels ? n : kProfKernels;
+  for (int i = 0; i < k; ++i) {
+    if (cudaEventElapsedTime(&ms_out[i], g_prof_ev[i], g_prof_ev[i + 1]) != cudaSuccess) return -MOE_ERR_CUDA;
+  }
+  return k;
+}
+
+const char* moe_fp8_ds_version(void) { return "moe_fp8_ds 0.1 sm_100a"; }
+
+}  // extern "C"

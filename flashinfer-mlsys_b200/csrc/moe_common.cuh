@@ -1,0 +1,248 @@
+// moe_common.cuh — geometry, workspace layout and sm_100a PTX helpers shared by
+// the fused FP8 DeepSeek-V3 MoE kernels.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace moe {
+
+// ---------------------------------------------------------------------------
+// Fixed DeepSeek-V3 geometry (reference moe/ref_moe.py:33-63, kernel.cu:25-33).
+// ---------------------------------------------------------------------------
+constexpr int kHidden = 7168;                 // H
+constexpr int kInter = 2048;                  // I
+constexpr int kGemm1N = 2 * kInter;           // 4096 rows of W13 (gate | up)
+constexpr int kExperts = 256;                 // global experts
+constexpr int kTopK = 8;
+constexpr int kGroups = 8;
+constexpr int kTopKGroups = 4;
+constexpr int kGroupSize = kExperts / kGroups;  // 32
+constexpr int kBlk = 128;                     // quantisation block
+constexpr int kHiddenBlocks = kHidden / kBlk; // 56
+constexpr int kInterBlocks = kInter / kBlk;   // 16
+constexpr int kGemm1NBlocks = kGemm1N / kBlk; // 32
+
+// ---------------------------------------------------------------------------
+// Tiling of the grouped GEMMs.
+//   A operand = token rows (M = 128 per tile, expert-major padded layout)
+//   B operand = expert weight rows (N = 256 per tile, two 128-row slabs)
+//   K step    = one 128-wide quantisation block per pipeline stage
+// GEMM1: N tile = 128 gate rows + the matching 128 up rows -> 16 N tiles,
+//        56 K blocks. GEMM2: N tile = 256 rows of W2 -> 28 N tiles,
+//        32 virtual K blocks (16 "hi" blocks + 16 "lo" blocks of the
+//        two-term FP8 intermediate, both against the same W2 block).
+// ---------------------------------------------------------------------------
+constexpr int kTileM = 128;
+constexpr int kTileN = 256;
+constexpr int kNT1 = kInter / kBlk;           // 16
+constexpr int kNT2 = kHidden / kTileN;        // 28
+constexpr int kKB1 = kHiddenBlocks;           // 56
+constexpr int kKB2 = 2 * kInterBlocks;        // 32
+constexpr int kInterCols = 2 * kInter;        // 4096 bytes per intermediate row (hi | lo)
+constexpr float kLoScale = 0.0625f;           // lo term scale = hi scale / 16
+
+constexpr int kStages = 4;
+constexpr int kStageA = kTileM * kBlk;        // 16 KB of e4m3
+constexpr int kStageB = kTileN * kBlk;        // 32 KB of e4m3
+constexpr int kStageBytes = kStageA + kStageB;
+
+constexpr int kGemmThreads = 576;             // 18 warps
+constexpr int kEpiWarp0 = 2;                  // warps 2..17 run the epilogue
+constexpr int kEpiWarps = 16;
+constexpr int kEpiThreads = kEpiWarps * 32;
+
+// Split-K of GEMM1 reduces fp32 partial tiles in a bounded scratch area.
+constexpr int kMaxSplitMTiles = 32;
+
+constexpr int kSMs = 148;
+
+// ---------------------------------------------------------------------------
+// Per-call plan written by the routing kernel's last CTA, read by the GEMMs.
+// ---------------------------------------------------------------------------
+struct Plan {
+  int total_mtiles;   // sum over local experts of ceil(count / 128)
+  int split1;         // K split of GEMM1 (1 = no split)
+  int split2;         // K split of GEMM2
+  int n_assign;       // number of (token, local expert) pairs
+  int mtile_prefix[kExperts + 1];  // first m-tile of each local expert
+  int count[kExperts];             // rows (tokens) of each local expert
+};
+
+// Status word bits written by kernels (never trap).
+constexpr unsigned kErrTimeout = 1u;
+
+// ---------------------------------------------------------------------------
+// PTX helpers (sm_100a).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: returns false (and the caller must abort) if the phase has
+// not completed within ~limit_ns of wall time.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = global_timer_ns();
+  uint32_t n = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++n & 255u) == 0u && global_timer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// 2D TMA tile load global -> shared, completion counted on `bar` (bytes).
+// No multicast: every CTA fetches its own tiles.
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---- tcgen05 (5th-generation tensor core, accumulators in TMEM) -----------
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, e4m3 x e4m3 -> f32, issued by one thread.
+__device__ __forceinline__ void mma_f8f6f4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once all previously issued tcgen05.mma of this thread complete.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns: thread i of the warp receives row
+// (lane base + i), columns [col, col+16). Waits for completion.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor for a K-major operand tile stored with the
+// 128-byte swizzle (rows of 128 bytes, 8-row / 1024-byte swizzle atoms).
+// Field layout (sm_100 UMMA descriptor): start address >> 4 in bits [0,14),
+// leading byte offset >> 4 in [16,30) (unused for swizzled K-major, set to 1),
+// stride byte offset >> 4 in [32,46) (1024 B between 8-row groups),
+// descriptor version 1 in [46,48), layout type 2 (SWIZZLE_128B) in [61,64).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f8f6f4: D f32, A e4m3, B e4m3, both
+// K-major, shape M x N. Bits: c_format [4,6)=1 (f32), a_format [7,10)=0,
+// b_format [10,13)=0, a_major bit 15 = 0, b_major bit 16 = 0,
+// N >> 3 in [17,23), M >> 4 in [24,29).
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// ---- misc -----------------------------------------------------------------
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// e4m3 conversion of two floats (round to nearest even, saturating).
+__device__ __forceinline__ uint16_t f2_to_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("{\n\t.reg .b16 t;\n\tcvt.rn.satfinite.e4m3x2.f32 t, %2, %1;\n\tmov.b16 %0, t;\n\t}"
+      : "=h"(r)
+      : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
+  // exact decode of one e4m3 byte via the packed converter
+  uint16_t in = b;
+  uint32_t h2;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(in));
+  __half_raw hr;
+  hr.x = static_cast<unsigned short>(h2 & 0xFFFFu);
+  return __half2float(__half(hr));
+}
+
+}  // namespace moe

@@ -1,0 +1,454 @@
+// moe_gemm.cu — K2/K3: persistent grouped block-scaled FP8 GEMMs on tcgen05.
+//
+//   GEMM1 (kMode = 1): G[r, :] = A1[r, :] (e4m3, 1x128 scales) x W13[e]^T
+//     (e4m3, 128x128 scales), K = 7168, then SwiGLU (ref_moe.py:153-159:
+//     C = G[:, :2048] * silu(G[:, 2048:]), silu(x) = x / (1 + exp(-x))) and
+//     re-quantisation of C into a two-term e4m3 intermediate per 1x128 block:
+//     hi = e4m3(C / s), lo = e4m3((C / s - hi) * 16), s = amax / 448, so
+//     C ~= s * hi + (s / 16) * lo.
+//   GEMM2 (kMode = 2): O[r, :] = Inter[r, :] x W2[e]^T over 32 virtual K
+//     blocks (16 hi + 16 lo, both against the same W2 block), then
+//     accum[token(r), :] += routing_weight(r) * O[r, :]  (ref_moe.py:162-166).
+//
+// Warp roles (576 threads, one CTA per SM):
+//   warp 0      TMA producer (one elected lane): A tile 128x128 + two B slabs
+//               128x128 per K block into a 4-stage shared-memory ring.
+//   warp 1      TMEM owner + MMA issuer (one lane): 4 x tcgen05.mma
+//               (M128 N256 K32, e4m3 x e4m3 -> f32) per K block into one of
+//               two 256-column TMEM partial accumulators.
+//   warps 2-17  epilogue: per K block, read the fresh partial from TMEM and
+//               promote it in fp32 registers with a_scale[row,kb] *
+//               w_scale[nblk,kb] (the block scales are arbitrary fp32, so no
+//               hardware block-scale mode applies); after the last K block
+//               run the fused output stage.
+// Work units (expert, m-tile, n-tile, k-split) come from the device-side plan
+// written by the routing kernel; CTAs walk them with a static stride.
+#include "moe_kernels.h"
+
+namespace moe {
+
+namespace {
+
+struct GemmArgs {
+  const Plan* plan;
+  const float* a_scale;     // GEMM1: [56][rows_cap]; GEMM2: [16][rows_cap]
+  const float* w_scale;     // GEMM1: [E_l][32][56];  GEMM2: [E_l][56][16]
+  int rows_cap;
+  int e_local;
+  uint8_t* inter;           // GEMM1 out: [rows_cap][4096]
+  float* inter_scale;       // GEMM1 out: [16][rows_cap]
+  float* g_part;            // GEMM1 split-K scratch: [kMaxSplitMTiles*128][4096]
+  int32_t* tile_sem;        // GEMM1 split-K counters: [kMaxSplitMTiles][16]
+  const int32_t* row_token; // GEMM2
+  const float* row_weight;  // GEMM2
+  float* accum;             // GEMM2 out: [T][7168]
+  unsigned* status;
+};
+
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: only reached if something is broken
+
+struct Unit {
+  int e, m, n, gm, kb0, kb1, rows;
+};
+
+template <int kMode>
+__device__ __forceinline__ Unit decode_unit(int u, int split, const int* prefix, const int* count, int e_local) {
+  constexpr int NT = (kMode == 1) ? kNT1 : kNT2;
+  constexpr int NKB = (kMode == 1) ? kKB1 : kKB2;
+  Unit x;
+  const int ks = u % split;
+  const int tile = u / split;
+  x.n = tile % NT;
+  x.gm = tile / NT;
+  // last expert whose first m-tile is <= gm (empty experts share prefixes)
+  int lo = 0, hi = e_local - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (prefix[mid] <= x.gm) lo = mid; else hi = mid - 1;
+  }
+  x.e = lo;
+  x.m = x.gm - prefix[lo];
+  x.rows = min(kTileM, count[lo] - x.m * kTileM);
+  x.kb0 = (ks * NKB) / split;
+  x.kb1 = ((ks + 1) * NKB) / split;
+  return x;
+}
+
+struct __align__(8) SmemCtl {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t mma_done;
+  uint64_t epi_bar;   // barrier among the 16 epilogue warps (bounded waits)
+  uint32_t tmem_base;
+  int abort_flag;
+  int fixup_flag;
+  int prefix[kExperts + 1];
+  int count[kExperts];
+  float amax[4][kTileM];
+};
+
+__device__ __forceinline__ void signal_abort(SmemCtl* c, unsigned* status) {
+  atomicOr(status, kErrTimeout);
+  *reinterpret_cast<volatile int*>(&c->abort_flag) = 1;
+}
+__device__ __forceinline__ bool aborted(SmemCtl* c) { return *reinterpret_cast<volatile int*>(&c->abort_flag) != 0; }
+
+// Barrier among the epilogue warps built on an mbarrier so that every wait is
+// bounded (a plain bar.sync could never give up). Returns false on timeout.
+struct EpiSync {
+  uint32_t phase = 0;
+  __device__ __forceinline__ bool sync(SmemCtl* c, unsigned* status) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&c->epi_bar);
+    bool ok = mbar_wait_bounded(&c->epi_bar, phase, kWaitLimitNs);
+    phase ^= 1u;
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) signal_abort(c, status);
+    return ok;
+  }
+};
+
+__device__ __forceinline__ float silu_ref(float x) { return x / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ float e4m3_byte_to_f32(uint32_t b) {
+  uint32_t h2;
+  asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(h2) : "r"(b));
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu)));
+}
+
+// SwiGLU of 32 (gate, up) pairs of one row + two-term e4m3 quantisation of the
+// 128-wide intermediate block shared by the 4 column-group warps of the row.
+__device__ __forceinline__ void swiglu_quant_store(const float* gate, const float* up, int cg, int row_in_tile,
+                                                   bool valid, size_t row, int n, SmemCtl* ctl,
+                                                   const GemmArgs& p, EpiSync& es) {
+  float c[32];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    c[i] = gate[i] * silu_ref(up[i]);
+    amax = fmaxf(amax, fabsf(c[i]));
+  }
+  ctl->amax[cg][row_in_tile] = amax;
+  if (!es.sync(ctl, p.status)) return;
+  amax = fmaxf(fmaxf(ctl->amax[0][row_in_tile], ctl->amax[1][row_in_tile]),
+               fmaxf(ctl->amax[2][row_in_tile], ctl->amax[3][row_in_tile]));
+  if (!es.sync(ctl, p.status)) return;
+  if (!valid) return;
+  const float inv = amax > 0.f ? 448.0f / amax : 0.f;
+  const float scale = amax / 448.0f;
+  uint32_t hi_w[8], lo_w[8];
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    uint32_t hw = 0, lw = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j += 2) {
+      const float u0 = c[i + j] * inv, u1 = c[i + j + 1] * inv;
+      const uint16_t h = f2_to_e4m3x2(u0, u1);
+      const float q0 = e4m3_byte_to_f32(h & 0xFFu), q1 = e4m3_byte_to_f32(h >> 8);
+      const uint16_t l = f2_to_e4m3x2((u0 - q0) * 16.0f, (u1 - q1) * 16.0f);
+      hw |= static_cast<uint32_t>(h) << (8 * j);
+      lw |= static_cast<uint32_t>(l) << (8 * j);
+    }
+    hi_w[i / 4] = hw;
+    lo_w[i / 4] = lw;
+  }
+  uint8_t* base = p.inter + row * kInterCols + n * kBlk + cg * 32;
+  uint4* dh = reinterpret_cast<uint4*>(base);
+  uint4* dl = reinterpret_cast<uint4*>(base + kInter);
+  dh[0] = make_uint4(hi_w[0], hi_w[1], hi_w[2], hi_w[3]);
+  dh[1] = make_uint4(hi_w[4], hi_w[5], hi_w[6], hi_w[7]);
+  dl[0] = make_uint4(lo_w[0], lo_w[1], lo_w[2], lo_w[3]);
+  dl[1] = make_uint4(lo_w[4], lo_w[5], lo_w[6], lo_w[7]);
+  if (cg == 0) p.inter_scale[(size_t)n * p.rows_cap + row] = scale;
+}
+
+template <int kMode>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+                    GemmArgs p) {
+  constexpr int NT = (kMode == 1) ? kNT1 : kNT2;
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment (in the shared window) for the 128-byte-swizzled tiles
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* tiles = smem;
+  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem + kStages * kStageBytes);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int E_l = p.e_local;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&ctl->full[s], 1);
+      mbar_init(&ctl->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ctl->tfull[b], 1);
+      mbar_init(&ctl->tempty[b], kEpiWarps);
+    }
+    mbar_init(&ctl->mma_done, 1);
+    mbar_init(&ctl->epi_bar, kEpiWarps);
+    ctl->abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tensormap(&map_a);
+    prefetch_tensormap(&map_w);
+  }
+  for (int e = tid; e <= E_l; e += blockDim.x) ctl->prefix[e] = p.plan->mtile_prefix[e];
+  for (int e = tid; e < E_l; e += blockDim.x) ctl->count[e] = p.plan->count[e];
+  if (warp == 1) {
+    tmem_alloc(&ctl->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const int total_mtiles = p.plan->total_mtiles;
+  const int split = (kMode == 1) ? p.plan->split1 : p.plan->split2;
+  const int units = total_mtiles * NT * split;
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (warp == 0) {
+    // ======================= TMA producer =======================
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int u = blockIdx.x; u < units && !aborted(ctl); u += gridDim.x) {
+        const Unit x = decode_unit<kMode>(u, split, ctl->prefix, ctl->count, E_l);
+        for (int kb = x.kb0; kb < x.kb1; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1u;
+          if (!mbar_wait_bounded(&ctl->empty[s], ph ^ 1u, kWaitLimitNs)) { signal_abort(ctl, p.status); break; }
+          uint8_t* sa = tiles + s * kStageBytes;
+          uint8_t* sb = sa + kStageA;
+          mbar_arrive_expect_tx(&ctl->full[s], kStageBytes);
+          tma_load_2d(sa, &map_a, kb * kBlk, x.gm * kTileM, &ctl->full[s]);
+          if (kMode == 1) {
+            const int y0 = x.e * kGemm1N + x.n * kBlk;
+            tma_load_2d(sb, &map_w, kb * kBlk, y0, &ctl->full[s]);
+            tma_load_2d(sb + kStageA, &map_w, kb * kBlk, y0 + kInter, &ctl->full[s]);
+          } else {
+            const int y0 = x.e * kHidden + x.n * kTileN;
+            const int kx = (kb % kInterBlocks) * kBlk;
+            tma_load_2d(sb, &map_w, kx, y0, &ctl->full[s]);
+            tma_load_2d(sb + kStageA, &map_w, kx, y0 + kBlk, &ctl->full[s]);
+          }
+        }
+        if (aborted(ctl)) break;
+      }
+      if (aborted(ctl)) {
+        // drain: wait (bounded) for the loads this thread may still have in flight
+        const uint32_t n_issued = it;
+        for (uint32_t j = (n_issued > kStages ? n_issued - kStages : 0); j < n_issued; ++j)
+          mbar_wait_bounded(&ctl->full[j % kStages], (j / kStages) & 1u, kWaitLimitNs);
+      }
+    }
+  } else if (warp == 1) {
+    // ======================= MMA issuer =======================
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_e4m3_f32(kTileM, kTileN);
+      uint32_t it = 0, gkb = 0;
+      bool issued_any = false;
+      for (int u = blockIdx.x; u < units && !aborted(ctl); u += gridDim.x) {
+        const Unit x = decode_unit<kMode>(u, split, ctl->prefix, ctl->count, E_l);
+        for (int kb = x.kb0; kb < x.kb1; ++kb, ++it, ++gkb) {
+          const uint32_t buf = gkb & 1u;
+          if (!mbar_wait_bounded(&ctl->tempty[buf], ((gkb >> 1) & 1u) ^ 1u, kWaitLimitNs)) {
+            signal_abort(ctl, p.status);
+            break;
+          }
+          const int s = it % kStages;
+          if (!mbar_wait_bounded(&ctl->full[s], (it / kStages) & 1u, kWaitLimitNs)) {
+            signal_abort(ctl, p.status);
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(tiles + s * kStageBytes);
+          const uint32_t sb = sa + kStageA;
+          const uint64_t da = smem_desc_sw128(sa), db = smem_desc_sw128(sb);
+#pragma unroll
+          for (int k = 0; k < kBlk / 32; ++k) {
+            // advance 32 bytes (one K=32 slice) inside the swizzle atom
+            mma_f8f6f4(tmem + buf * kTileN, da + 2 * k, db + 2 * k, idesc, k > 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          mma_commit(&ctl->empty[s]);
+          mma_commit(&ctl->tfull[buf]);
+        }
+        if (aborted(ctl)) break;
+      }
+      if (aborted(ctl) && issued_any) {
+        mma_commit(&ctl->mma_done);
+        mbar_wait_bounded(&ctl->mma_done, 0, kWaitLimitNs);
+      }
+    }
+  } else {
+    // ======================= epilogue (16 warps) =======================
+    const int q = warp & 3;              // TMEM lane quarter accessible to this warp
+    const int cg = (warp - kEpiWarp0) >> 2;  // column group 0..3
+    const int row_in_tile = q * 32 + lane;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    uint32_t gkb = 0;
+    EpiSync es;
+    float acc[64];
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      if (aborted(ctl)) break;
+      const Unit x = decode_unit<kMode>(u, split, ctl->prefix, ctl->count, E_l);
+      const size_t row = (size_t)x.gm * kTileM + row_in_tile;
+      const bool valid = row_in_tile < x.rows;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+      bool ok = true;
+      for (int kb = x.kb0; kb < x.kb1; ++kb, ++gkb) {
+        const uint32_t buf = gkb & 1u;
+        float f0, f1;
+        if (kMode == 1) {
+          const float as = __ldg(p.a_scale + (size_t)kb * p.rows_cap + row);
+          const float* ws = p.w_scale + (size_t)x.e * (kGemm1NBlocks * kHiddenBlocks);
+          f0 = as * __ldg(ws + x.n * kHiddenBlocks + kb);
+          f1 = as * __ldg(ws + (kNT1 + x.n) * kHiddenBlocks + kb);
+        } else {
+          const int kr = kb % kInterBlocks;
+          float as = __ldg(p.a_scale + (size_t)kr * p.rows_cap + row);
+          if (kb >= kInterBlocks) as *= kLoScale;
+          const int nb = 2 * x.n + (cg >> 1);
+          f0 = f1 = as * __ldg(p.w_scale + ((size_t)x.e * kHiddenBlocks + nb) * kInterBlocks + kr);
+        }
+        const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(&ctl->tfull[buf], (gkb >> 1) & 1u, kWaitLimitNs));
+        if (!got) {
+          signal_abort(ctl, p.status);
+          ok = false;
+          break;
+        }
+        __syncwarp();
+        tc_fence_after();
+        const uint32_t tb = t_lane + buf * kTileN;
+        // columns of this warp: GEMM1 gate [32cg, 32cg+32) and up [128+32cg, ...);
+        // GEMM2 [64cg, 64cg+64)
+        const uint32_t c0 = (kMode == 1) ? cg * 32 : cg * 64;
+        const uint32_t c1 = (kMode == 1) ? kBlk + cg * 32 : cg * 64 + 32;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          float v[16];
+          const uint32_t col = (h < 2) ? c0 + 16 * h : c1 + 16 * (h - 2);
+          const float f = (h < 2) ? f0 : f1;
+          tmem_ld_32x32b_x16(tb + col, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc[16 * h + i] = fmaf(f, v[i], acc[16 * h + i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->tempty[buf]);
+      }
+      if (!ok) break;
+
+      if (kMode == 1) {
+        if (split == 1) {
+          swiglu_quant_store(acc, acc + 32, cg, row_in_tile, valid, row, x.n, ctl, p, es);
+        } else {
+          // split-K: reduce promoted partials in fp32 scratch; the last
+          // arriving CTA of this (m-tile, n-tile) runs SwiGLU + quantisation.
+          float* g = p.g_part + row * kGemm1N;
+          if (valid) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              red_add_v4(g + x.n * kBlk + cg * 32 + i, acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+              red_add_v4(g + kInter + x.n * kBlk + cg * 32 + i, acc[32 + i], acc[33 + i], acc[34 + i],
+                         acc[35 + i]);
+            }
+          }
+          __threadfence();
+          if (!es.sync(ctl, p.status)) break;
+          if (warp == kEpiWarp0 && lane == 0) {
+            const int old = atomicAdd(&p.tile_sem[x.gm * kNT1 + x.n], 1);
+            ctl->fixup_flag = (old == split - 1) ? 1 : 0;
+          }
+          if (!es.sync(ctl, p.status)) break;
+          if (ctl->fixup_flag) {
+            __threadfence();
+            if (valid) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 4) {
+                float4* pg = reinterpret_cast<float4*>(g + x.n * kBlk + cg * 32 + i);
+                float4* pu = reinterpret_cast<float4*>(g + kInter + x.n * kBlk + cg * 32 + i);
+                const float4 a4 = __ldcg(pg), b4 = __ldcg(pu);
+                acc[i] = a4.x; acc[i + 1] = a4.y; acc[i + 2] = a4.z; acc[i + 3] = a4.w;
+                acc[32 + i] = b4.x; acc[33 + i] = b4.y; acc[34 + i] = b4.z; acc[35 + i] = b4.w;
+                __stcg(pg, make_float4(0.f, 0.f, 0.f, 0.f));
+                __stcg(pu, make_float4(0.f, 0.f, 0.f, 0.f));
+              }
+            }
+            swiglu_quant_store(acc, acc + 32, cg, row_in_tile, valid, row, x.n, ctl, p, es);
+            if (warp == kEpiWarp0 && lane == 0) p.tile_sem[x.gm * kNT1 + x.n] = 0;
+          }
+        }
+      } else {
+        if (valid) {
+          const int tok = __ldg(p.row_token + row);
+          const float w = __ldg(p.row_weight + row);
+          float* dst = p.accum + (size_t)tok * kHidden + x.n * kTileN + cg * 64;
+#pragma unroll
+          for (int i = 0; i < 64; i += 4)
+            red_add_v4(dst + i, w * acc[i], w * acc[i + 1], w * acc[i + 2], w * acc[i + 3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+size_t gemm_smem_bytes() { return kStages * kStageBytes + sizeof(SmemCtl) + 1024; }
+
+template <int kMode>
+cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
+                        const float* w_scale, cudaStream_t s) {
+  static int configured[2] = {0, 0};
+  const size_t smem = gemm_smem_bytes();
+  if (!configured[kMode - 1]) {
+    cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<kMode>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured[kMode - 1] = 1;
+  }
+  int dev = 0, sms = kSMs;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  GemmArgs p{};
+  p.plan = ws.plan;
+  p.a_scale = (kMode == 1) ? ws.a1_scale : ws.inter_scale;
+  p.w_scale = w_scale;
+  p.rows_cap = static_cast<int>(ws.rows_cap);
+  p.e_local = ws.e_local;
+  p.inter = ws.inter;
+  p.inter_scale = ws.inter_scale;
+  p.g_part = ws.g_part;
+  p.tile_sem = ws.tile_sem;
+  p.row_token = ws.row_token;
+  p.row_weight = ws.row_weight;
+  p.accum = ws.accum;
+  p.status = ws.status;
+  moe_gemm_kernel<kMode><<<sms, kGemmThreads, smem, s>>>(map_a, map_w, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
+                         const float* w_scale, cudaStream_t s) {
+  return launch_gemm<1>(ws, map_a, map_w, w_scale, s);
+}
+
+cudaError_t launch_gemm2(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
+                         const float* w_scale, cudaStream_t s) {
+  return launch_gemm<2>(ws, map_a, map_w, w_scale, s);
+}
+
+}  // namespace moe

@@ -1,0 +1,293 @@
+// moe_route.cu — K1 (DeepSeek-V3 no-aux routing + local histogram + plan),
+// K1b (token permutation into the expert-major padded layout) and K4
+// (fp32 combine accumulator -> bf16/fp32 output).
+//
+// Routing semantics follow reference moe/ref_moe.py:95-126:
+//   s = 1 / (1 + exp(-logit)); sb = s + bias
+//   group score = sum of the two largest sb in each of 8 groups of 32
+//   keep the 4 best groups; take the 8 largest sb inside them
+//   weight_k = s[id_k] / (sum_k s[id_k] + 1e-20) * routed_scaling_factor
+// and the local dispatch of ref_moe.py:131-148 / kernel.cu:201-232
+// (expert id - local_expert_offset in [0, E_local)).
+#include "moe_kernels.h"
+
+namespace moe {
+
+namespace {
+
+constexpr int kRouteThreads = 256;  // 8 warps, one token per warp at a time
+
+struct Cand {
+  float v;   // sb (selection key)
+  float s;   // un-biased sigmoid (weight numerator)
+  int idx;   // global expert id
+};
+
+// a beats b: larger key, ties to the smaller expert id.
+__device__ __forceinline__ bool beats(float av, int ai, float bv, int bi) {
+  return av > bv || (av == bv && ai < bi);
+}
+
+__global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, Workspace ws) {
+  __shared__ int hist[kExperts];
+  __shared__ int is_last;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int E_l = a.e_local;
+  for (int e = tid; e < E_l; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
+
+  const int t_begin = blockIdx.x * a.tokens_per_cta;
+  const int t_end = min(a.T, t_begin + a.tokens_per_cta);
+  for (int t = t_begin + warp; t < t_end; t += kRouteThreads / 32) {
+    int my_id = -1;     // lane k < 8 holds the k-th selected expert
+    float my_w = 0.f;
+    if (a.logits != nullptr) {
+      // ---- lane l owns experts [8l, 8l+8): group g = l / 4 ----
+      const float4* lp = reinterpret_cast<const float4*>(a.logits + (size_t)t * kExperts + lane * 8);
+      float4 x0 = __ldg(lp), x1 = __ldg(lp + 1);
+      float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+      uint4 braw = __ldg(reinterpret_cast<const uint4*>(a.bias + lane * 8));
+      const uint32_t bw[4] = {braw.x, braw.y, braw.z, braw.w};
+      float s[8], sb[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        uint32_t bits = (i & 1) ? (bw[i >> 1] & 0xFFFF0000u) : (bw[i >> 1] << 16);
+        float b = __uint_as_float(bits);
+        s[i] = 1.0f / (1.0f + expf(-x[i]));
+        sb[i] = s[i] + b;
+      }
+      // ---- top-2 of the group (4 lanes) ----
+      float m1 = -INFINITY, m2 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float v = sb[i];
+        if (v > m1) { m2 = m1; m1 = v; } else if (v > m2) { m2 = v; }
+      }
+#pragma unroll
+      for (int off = 1; off <= 2; off <<= 1) {
+        float o1 = __shfl_xor_sync(0xffffffffu, m1, off);
+        float o2 = __shfl_xor_sync(0xffffffffu, m2, off);
+        float n1 = fmaxf(m1, o1);
+        float n2 = fmaxf(fminf(m1, o1), fmaxf(m2, o2));
+        m1 = n1; m2 = n2;
+      }
+      const float gscore = m1 + m2;
+      const int g = lane >> 2;
+      int rank = 0;
+#pragma unroll
+      for (int gg = 0; gg < kGroups; ++gg) {
+        float o = __shfl_sync(0xffffffffu, gscore, gg * 4);
+        rank += (o > gscore || (o == gscore && gg < g)) ? 1 : 0;
+      }
+      const bool kept = rank < kTopKGroups;
+      float key[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) key[i] = kept ? sb[i] : -INFINITY;
+      // ---- 8 rounds of warp arg-max over the kept candidates ----
+      float ssum = 0.f;
+      float sel_s = 0.f;
+#pragma unroll 1
+      for (int k = 0; k < kTopK; ++k) {
+        Cand c{-INFINITY, 0.f, 0x7fffffff};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (beats(key[i], lane * 8 + i, c.v, c.idx)) { c.v = key[i]; c.s = s[i]; c.idx = lane * 8 + i; }
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+          float ov = __shfl_xor_sync(0xffffffffu, c.v, off);
+          float os = __shfl_xor_sync(0xffffffffu, c.s, off);
+          int oi = __shfl_xor_sync(0xffffffffu, c.idx, off);
+          if (beats(ov, oi, c.v, c.idx)) { c.v = ov; c.s = os; c.idx = oi; }
+        }
+        if ((c.idx >> 3) == lane) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (i == (c.idx & 7)) key[i] = -INFINITY;
+        }
+        if (lane == k) { my_id = c.idx; sel_s = c.s; }
+        ssum += c.s;
+      }
+      my_w = (sel_s / (ssum + 1e-20f)) * a.scale;
+    } else if (lane < kTopK) {
+      my_id = __ldg(a.given_ids + (size_t)t * kTopK + lane);
+      my_w = __ldg(a.given_w + (size_t)t * kTopK + lane);
+    }
+    if (lane < kTopK) {
+      const size_t o = (size_t)t * kTopK + lane;
+      ws.topk_ids[o] = my_id;
+      ws.topk_w[o] = my_w;
+      if (a.user_ids) a.user_ids[o] = my_id;
+      if (a.user_w) a.user_w[o] = my_w;
+      const int le = my_id - a.offset;
+      int r = -1;
+      if (my_id >= 0 && le >= 0 && le < E_l) r = atomicAdd(&hist[le], 1);
+      ws.topk_rank[o] = r;
+    }
+  }
+  __syncthreads();
+
+  // ---- publish this CTA's histogram: its base slot inside every expert ----
+  for (int e = tid; e < E_l; e += blockDim.x) {
+    const int h = hist[e];
+    ws.cta_off[(size_t)blockIdx.x * E_l + e] = h ? atomicAdd(&ws.expert_fill[e], h) : 0;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) is_last = (atomicAdd(ws.done_ctas, 1u) == gridDim.x - 1) ? 1 : 0;
+  __syncthreads();
+  if (!is_last) return;
+
+  // ---- last CTA: per-expert counts, m-tile prefix, K-split plan ----
+  __threadfence();
+  __shared__ int mt[kExperts + 1];
+  for (int e = tid; e < kExperts; e += blockDim.x) {
+    int c = 0;
+    if (e < E_l) {
+      c = atomicExch(&ws.expert_fill[e], 0);  // read and reset for the next call
+      ws.plan->count[e] = c;
+      if (a.user_counts) a.user_counts[e] = c;
+    }
+    hist[e] = c;
+    mt[e] = (c + kTileM - 1) / kTileM;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int run = 0, nas = 0;
+    for (int e = 0; e < E_l; ++e) {
+      ws.plan->mtile_prefix[e] = run;
+      run += mt[e];
+      nas += hist[e];
+    }
+    ws.plan->mtile_prefix[E_l] = run;
+    ws.plan->total_mtiles = run;
+    ws.plan->n_assign = nas;
+    // K split: minimise waves * (k-blocks per unit + per-unit overhead).
+    auto pick = [&](int tiles, int nkb, int smax) {
+      if (tiles <= 0) return 1;
+      int best = 1;
+      long best_cost = 0x7fffffffffffL;
+      for (int sp = 1; sp <= smax; ++sp) {
+        long units = (long)tiles * sp;
+        long waves = (units + kSMs - 1) / kSMs;
+        long cost = waves * ((nkb + sp - 1) / sp + 3);
+        if (cost < best_cost) { best_cost = cost; best = sp; }
+      }
+      return best;
+    };
+    ws.plan->split1 = (run <= kMaxSplitMTiles) ? pick(run * kNT1, kKB1, 14) : 1;
+    ws.plan->split2 = pick(run * kNT2, kKB2, 8);
+    *ws.done_ctas = 0u;
+  }
+}
+
+// One warp per token: copy the e4m3 row (7168 B) and its 56 block scales to
+// every local expert slot the token was routed to.
+__global__ void __launch_bounds__(256) permute_kernel(PermuteArgs a, Workspace ws) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= a.T) return;
+  const int E_l = ws.e_local;
+  int row = -1;
+  float w = 0.f;
+  if (lane < kTopK) {
+    const size_t o = (size_t)t * kTopK + lane;
+    const int r = ws.topk_rank[o];
+    if (r >= 0) {
+      const int le = ws.topk_ids[o] - a.offset;
+      const int cta = t / a.tokens_per_cta;
+      row = ws.plan->mtile_prefix[le] * kTileM + ws.cta_off[(size_t)cta * E_l + le] + r;
+      w = ws.topk_w[o];
+    }
+  }
+  const unsigned has = __ballot_sync(0xffffffffu, row >= 0);
+  if (!has) return;
+  const uint4* src = reinterpret_cast<const uint4*>(a.hidden + (size_t)t * kHidden);
+  uint4 v[kHidden / 16 / 32];  // 14 chunks of 16 B per lane
+#pragma unroll
+  for (int i = 0; i < kHidden / 16 / 32; ++i) v[i] = __ldg(src + lane + 32 * i);
+  const float sc0 = __ldg(a.hidden_scale + (size_t)lane * a.T + t);
+  const float sc1 = (lane + 32 < kHiddenBlocks) ? __ldg(a.hidden_scale + (size_t)(lane + 32) * a.T + t) : 0.f;
+  unsigned m = has;
+  while (m) {
+    const int k = __ffs(m) - 1;
+    m &= m - 1;
+    const int r = __shfl_sync(0xffffffffu, row, k);
+    const float wk = __shfl_sync(0xffffffffu, w, k);
+    uint4* dst = reinterpret_cast<uint4*>(ws.a1 + (size_t)r * kHidden);
+#pragma unroll
+    for (int i = 0; i < kHidden / 16 / 32; ++i) dst[lane + 32 * i] = v[i];
+    ws.a1_scale[(size_t)lane * ws.rows_cap + r] = sc0;
+    if (lane + 32 < kHiddenBlocks) ws.a1_scale[(size_t)(lane + 32) * ws.rows_cap + r] = sc1;
+    if (lane == 0) {
+      ws.row_token[r] = t;
+      ws.row_weight[r] = wk;
+    }
+  }
+}
+
+// out = cast(accum); accum = 0. Eight elements per thread.
+__global__ void __launch_bounds__(256) finalize_kernel(float* __restrict__ accum, void* __restrict__ out,
+                                                       int64_t n8, int out_fp32) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    float4* p = reinterpret_cast<float4*>(accum) + 2 * i;
+    float4 x0 = p[0], x1 = p[1];
+    p[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    p[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (out_fp32) {
+      float4* o = reinterpret_cast<float4*>(out) + 2 * i;
+      o[0] = x0;
+      o[1] = x1;
+    } else {
+      __nv_bfloat162 b0 = __floats2bfloat162_rn(x0.x, x0.y);
+      __nv_bfloat162 b1 = __floats2bfloat162_rn(x0.z, x0.w);
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(x1.x, x1.y);
+      __nv_bfloat162 b3 = __floats2bfloat162_rn(x1.z, x1.w);
+      uint4 u;
+      u.x = *reinterpret_cast<uint32_t*>(&b0);
+      u.y = *reinterpret_cast<uint32_t*>(&b1);
+      u.z = *reinterpret_cast<uint32_t*>(&b2);
+      u.w = *reinterpret_cast<uint32_t*>(&b3);
+      reinterpret_cast<uint4*>(out)[i] = u;
+    }
+  }
+}
+
+}  // namespace
+
+int tokens_per_cta_for(int T) {
+  // one token per warp for small T; at most ~kSMs routing CTAs for large T
+  int per = (T + kSMs - 1) / kSMs;
+  per = ((per + 7) / 8) * 8;
+  return per < 8 ? 8 : per;
+}
+
+int route_ctas_for(int T) {
+  if (T <= 0) return 1;
+  const int per = tokens_per_cta_for(T);
+  return (T + per - 1) / per;
+}
+
+cudaError_t launch_route(const Workspace& ws, const RouteArgs& a, cudaStream_t s) {
+  const int grid = route_ctas_for(a.T);
+  route_plan_kernel<<<grid, kRouteThreads, 0, s>>>(a, ws);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_permute(const Workspace& ws, const PermuteArgs& a, cudaStream_t s) {
+  if (a.T <= 0) return cudaSuccess;
+  permute_kernel<<<(a.T + 7) / 8, 256, 0, s>>>(a, ws);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32, cudaStream_t s) {
+  const int64_t n8 = (int64_t)T * kHidden / 8;
+  if (n8 == 0) return cudaSuccess;
+  int64_t blocks = (n8 + 255) / 256;
+  if (blocks > 8 * kSMs) blocks = 8 * kSMs;
+  finalize_kernel<<<(int)blocks, 256, 0, s>>>(ws.accum, out, n8, out_fp32);
+  return cudaGetLastError();
+}
+
+}  // namespace moe

@@ -1,0 +1,154 @@
+/*
+ * moe_fp8_ds.h — C ABI of the B200 (sm_100a) fused FP8 DeepSeek-V3 MoE layer.
+ *
+ * Operator: moe_fp8_block_scale_ds_routing_topk8_ng8_kg4_e32_h7168_i2048
+ * (reference definition: "reference moe/ref_moe.json", semantics:
+ * "reference moe/ref_moe.py:5-167").
+ *
+ * All pointers are DEVICE pointers unless stated otherwise; all tensors are
+ * contiguous row-major. Byte types: e4m3 tensors are passed as `const void*`
+ * (one byte per element, float8_e4m3fn bit pattern), bf16 tensors as
+ * `const void*` / `void*` (two bytes per element). Every call is enqueued on
+ * `stream` (a cudaStream_t, NULL = legacy default stream) and returns without
+ * synchronising the host; errors detected before launch are returned as a
+ * status code and nothing is launched. The library caches its device
+ * workspace per device (grown on demand with cudaMalloc on the first call of
+ * a larger size), so calls on one device must be stream-ordered with respect
+ * to each other.
+ *
+ * Fixed geometry: hidden 7168, intermediate 2048, 256 global experts, top-8,
+ * 8 groups, top-4 groups, 128x128 / 1x128 quantisation blocks.
+ */
+#ifndef MOE_FP8_DS_H_
+#define MOE_FP8_DS_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by every entry point. */
+#define MOE_OK 0
+#define MOE_ERR_INVALID_ARG 1   /* bad size, null pointer or unsupported value */
+#define MOE_ERR_ALIGNMENT 2     /* a tensor base is not 16-byte aligned          */
+#define MOE_ERR_CUDA 3          /* a CUDA runtime/driver call failed             */
+#define MOE_ERR_NO_DEVICE 4     /* no sm_100 device current                      */
+#define MOE_ERR_WORKSPACE 5     /* workspace allocation failed                   */
+#define MOE_ERR_DEVICE_TIMEOUT 6 /* a bounded device-side wait gave up (read by moe_fp8_ds_device_status) */
+
+/*
+ * The drop-in entry point. Replaces the destination-passing `kernel(...)` of
+ * solution/cuda/kernel.cu:134-146 (bound to Python at kernel.cu:296-298 and
+ * wrapped by solution/cuda/binding.py:149-161). Same 11 arguments in the same
+ * order and meaning, plus the sizes a C ABI cannot infer from tensors and the
+ * stream:
+ *   routing_logits      f32  [seq_len, 256]
+ *   routing_bias        bf16 [256]
+ *   hidden_states       e4m3 [seq_len, 7168]
+ *   hidden_states_scale f32  [56, seq_len]        (transposed block scales)
+ *   gemm1_weights       e4m3 [num_local_experts, 4096, 7168]
+ *   gemm1_weights_scale f32  [num_local_experts, 32, 56]
+ *   gemm2_weights       e4m3 [num_local_experts, 7168, 2048]
+ *   gemm2_weights_scale f32  [num_local_experts, 56, 16]
+ *   local_expert_offset first global expert id held by this rank
+ *   routed_scaling_factor
+ *   output              bf16 [seq_len, 7168]     (every element is written)
+ * num_local_experts is 32 for the reference definition; 64, 128 and 256 are
+ * accepted for expert-parallel layouts with fewer ranks. seq_len may be 0.
+ */
+int moe_fp8_ds_kernel(const float* routing_logits, const void* routing_bias,
+                      const void* hidden_states, const float* hidden_states_scale,
+                      const void* gemm1_weights, const float* gemm1_weights_scale,
+                      const void* gemm2_weights, const float* gemm2_weights_scale,
+                      int64_t local_expert_offset, double routed_scaling_factor,
+                      void* output, int64_t seq_len, int64_t num_local_experts,
+                      void* stream);
+
+/*
+ * Same as moe_fp8_ds_kernel, and additionally exposes the routing decision of
+ * this very call (any of the three may be NULL):
+ *   topk_ids_out       int32 [seq_len, 8]   global expert ids, best first
+ *   topk_weights_out   f32   [seq_len, 8]   normalised un-biased sigmoid x scale
+ *   expert_counts_out  int32 [num_local_experts] tokens routed to each local expert
+ * Reference counterpart: the routing/dispatch tensors topk_idx, weights and
+ * the per-expert counts of kernel.cu:175-232 / ref_moe.py:95-148.
+ */
+int moe_fp8_ds_kernel_ex(const float* routing_logits, const void* routing_bias,
+                         const void* hidden_states, const float* hidden_states_scale,
+                         const void* gemm1_weights, const float* gemm1_weights_scale,
+                         const void* gemm2_weights, const float* gemm2_weights_scale,
+                         int64_t local_expert_offset, double routed_scaling_factor,
+                         void* output, int64_t seq_len, int64_t num_local_experts,
+                         int32_t* topk_ids_out, float* topk_weights_out,
+                         int32_t* expert_counts_out, void* stream);
+
+/*
+ * Routing only: DeepSeek-V3 no-aux grouped top-k (ref_moe.py:95-126,
+ * kernel.cu:157-198) plus the local per-expert histogram (kernel.cu:201-232).
+ * Outputs as in moe_fp8_ds_kernel_ex; topk_ids_out and topk_weights_out are
+ * required, expert_counts_out may be NULL.
+ */
+int moe_fp8_ds_route(const float* routing_logits, const void* routing_bias,
+                     int64_t seq_len, int64_t local_expert_offset,
+                     int64_t num_local_experts, double routed_scaling_factor,
+                     int32_t* topk_ids_out, float* topk_weights_out,
+                     int32_t* expert_counts_out, void* stream);
+
+/*
+ * Expert computation for pre-routed tokens (the expert loop of
+ * kernel.cu:235-291 / ref_moe.py:131-167, without the routing step). Used by
+ * the expert-parallel layer on the rank that owns the experts:
+ *   hidden_states       e4m3 [num_rows, 7168], hidden_states_scale f32 [56, num_rows]
+ *   topk_ids            int32 [num_rows, 8] global expert ids (ids outside
+ *                       [local_expert_offset, +num_local_experts) are skipped)
+ *   topk_weights        f32 [num_rows, 8]
+ *   output              f32 [num_rows, 7168] if output_fp32 != 0, else bf16;
+ *                       row r = sum over its local experts of weight * expert(row r).
+ */
+int moe_fp8_ds_experts(const void* hidden_states, const float* hidden_states_scale,
+                       const int32_t* topk_ids, const float* topk_weights,
+                       const void* gemm1_weights, const float* gemm1_weights_scale,
+                       const void* gemm2_weights, const float* gemm2_weights_scale,
+                       int64_t local_expert_offset, int64_t num_rows,
+                       int64_t num_local_experts, void* output, int output_fp32,
+                       void* stream);
+
+/*
+ * Per-kernel timing of this library's launches (instrumentation; the
+ * reference times its kernels with CUDA events in scripts/ncu_profile.py:191-240).
+ * While enabled, every pipeline call records CUDA events on its own stream
+ * around each of its kernels. moe_fp8_ds_profile_last() synchronises on the
+ * last call's final event and writes the milliseconds of its kernels
+ * (route, permute, gemm1, gemm2, finalize) to ms_out[0..4]; returns the number
+ * written, or a negative status. Disabled by default; enabling costs one
+ * event record per kernel.
+ */
+int moe_fp8_ds_profile_enable(int on);
+int moe_fp8_ds_profile_last(float* ms_out, int n);
+
+/* Human-readable text for a status code (static storage, never NULL). */
+const char* moe_fp8_ds_status_string(int status);
+
+/*
+ * Synchronises `stream` and returns MOE_ERR_DEVICE_TIMEOUT if any kernel of
+ * this library gave up a bounded device-side wait since the last call of this
+ * function (and clears the flag), MOE_ERR_CUDA on a CUDA error, else MOE_OK.
+ */
+int moe_fp8_ds_device_status(void* stream);
+
+/* Bytes of device workspace the library holds for (seq_len, num_local_experts). */
+size_t moe_fp8_ds_workspace_bytes(int64_t seq_len, int64_t num_local_experts);
+
+/* Frees the cached workspace of the current device (next call re-allocates). */
+int moe_fp8_ds_release_workspace(void);
+
+/* Library version string, e.g. "moe_fp8_ds 0.1 sm_100a". */
+const char* moe_fp8_ds_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_FP8_DS_H_ */

@@ -1,0 +1,210 @@
+"""CPU oracle for the fused FP8 DeepSeek-V3 MoE layer — TEST INFRASTRUCTURE.
+
+This is a numpy restatement of the reference implementation
+``reference moe/ref_moe.py:run`` (vanshnawander/flashinfer-mlsys). It exists
+only to check the CUDA path: it is imported by ``tests/``, by
+``__graft_entry__.smoke()`` (as the checker) and by ``bench.py``'s CPU
+baseline leg. The product path never calls it.
+
+Pinned against golden vectors produced by running the reference's own
+``ref_moe.run`` on CPU (``tests/golden/make_golden.py``; fixtures in
+``tests/golden/*.npz``), see ``tests/test_oracle_golden.py``.
+
+Every step cites the reference line it follows. One deliberate deviation in
+cost, not in result: the reference dequantises all local experts up front
+(ref_moe.py:80-92) but only ever uses the experts some token selected
+(ref_moe.py:140-144); this oracle dequantises an expert only when it is used.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+H, I, E, BLOCK = 7168, 2048, 256, 128
+TOP_K, N_GROUP, TOPK_GROUP = 8, 8, 4
+GROUP_SIZE = E // N_GROUP
+
+
+def _e4m3_table() -> np.ndarray:
+    """float32 value of every e4m3fn byte (sign, 4-bit exponent bias 7,
+    3-bit mantissa; exponent 0 is subnormal; 0x7f/0xff are NaN)."""
+    t = np.zeros(256, dtype=np.float32)
+    for b in range(256):
+        s = -1.0 if b & 0x80 else 1.0
+        e = (b >> 3) & 0xF
+        m = b & 0x7
+        if e == 0xF and m == 0x7:
+            t[b] = np.nan
+        elif e == 0:
+            t[b] = s * (m / 8.0) * 2.0 ** -6
+        else:
+            t[b] = s * (1.0 + m / 8.0) * 2.0 ** (e - 7)
+    return t
+
+
+E4M3 = _e4m3_table()
+
+
+def as_u8(x) -> np.ndarray:
+    """numpy uint8 view of an e4m3 tensor (torch float8 or uint8 array)."""
+    if hasattr(x, "view") and hasattr(x, "dtype") and "float8" in str(x.dtype):
+        import torch  # only for the dtype view of torch inputs
+
+        return x.detach().cpu().view(torch.uint8).numpy()
+    return np.asarray(x, dtype=np.uint8)
+
+
+def as_f32(x) -> np.ndarray:
+    if hasattr(x, "detach"):
+        import torch
+
+        x = x.detach().cpu()
+        if x.dtype == torch.bfloat16:
+            return bf16_bits_to_f32(x.view(torch.int16).numpy().view(np.uint16))
+        return x.float().numpy()
+    return np.asarray(x, dtype=np.float32)
+
+
+def bf16_bits_to_f32(u16: np.ndarray) -> np.ndarray:
+    return (u16.astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even float32 -> bfloat16 bit pattern (what
+    ``Tensor.to(torch.bfloat16)`` does for finite values)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u >> 16) & 1) + 0x7FFF
+    out = ((u + r) >> 16).astype(np.uint16)
+    nan = np.isnan(x)
+    if nan.any():
+        out[nan] = 0x7FC0
+    return out
+
+
+def dequant_rows(q_u8: np.ndarray, scale_kt: np.ndarray) -> np.ndarray:
+    """ref_moe.py:69-78: A[t, h] = fp8[t, h] * scale[h // 128, t] (scale is [H/128, T])."""
+    T = q_u8.shape[0]
+    a = E4M3[q_u8].reshape(T, H // BLOCK, BLOCK)
+    return (a * scale_kt.T[:, :, None]).reshape(T, H)
+
+
+def dequant_blocks(q_u8: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    """ref_moe.py:80-92: W[n, k] = fp8[n, k] * S[n // 128, k // 128]."""
+    n, k = q_u8.shape
+    w = E4M3[q_u8].reshape(n // BLOCK, BLOCK, k // BLOCK, BLOCK)
+    return (w * scale[:, None, :, None]).reshape(n, k)
+
+
+def _topk_desc(x: np.ndarray, k: int) -> np.ndarray:
+    """Indices of the k largest entries per row, best first; equal values go
+    to the lower index (torch.topk leaves tie order unspecified)."""
+    return np.argsort(-x, axis=1, kind="stable")[:, :k]
+
+
+def route(logits: np.ndarray, bias: np.ndarray, routed_scaling_factor: float):
+    """DeepSeek-V3 no-aux routing, ref_moe.py:95-126.
+
+    Returns dict with topk_idx [T, 8] (best first), weights [T, 256] (the
+    reference's dense weight matrix), s, s_with_bias, group_scores, group_idx.
+    """
+    logits = np.asarray(logits, dtype=np.float32)
+    bias = np.asarray(bias, dtype=np.float32).reshape(-1)
+    T = logits.shape[0]
+    one = np.float32(1.0)
+    s = one / (one + np.exp(-logits))                                   # :99
+    sb = (s + bias).astype(np.float32)                                  # :100
+    grouped = sb.reshape(T, N_GROUP, GROUP_SIZE)                        # :104
+    top2 = -np.sort(-grouped, axis=2)[:, :, :2]                         # :107
+    group_scores = (top2[:, :, 0] + top2[:, :, 1]).astype(np.float32)   # :108
+    group_idx = _topk_desc(group_scores, TOPK_GROUP)                    # :111
+    group_mask = np.zeros((T, N_GROUP), dtype=np.float32)               # :112
+    np.put_along_axis(group_mask, group_idx, 1.0, axis=1)               # :113
+    score_mask = np.repeat(group_mask, GROUP_SIZE, axis=1)              # :114
+    neg = np.float32(np.finfo(np.float32).min)                          # :117
+    pruned = np.where(score_mask == 0, neg, sb)                         # :118
+    topk_idx = _topk_desc(pruned, TOP_K)                                # :119
+    M = np.zeros_like(s)                                                # :122
+    np.put_along_axis(M, topk_idx, 1.0, axis=1)                         # :123
+    w = s * M                                                           # :124
+    wsum = w.sum(axis=1, keepdims=True, dtype=np.float32) + np.float32(1e-20)  # :125
+    w = (w / wsum) * np.float32(routed_scaling_factor)                 # :126
+    return {
+        "topk_idx": topk_idx, "weights": w.astype(np.float32), "s": s, "s_with_bias": sb,
+        "group_scores": group_scores, "group_idx": group_idx, "pruned": pruned,
+    }
+
+
+def local_counts(topk_idx: np.ndarray, offset: int, e_local: int) -> np.ndarray:
+    """Tokens per local expert (ref_moe.py:131-144 selection rule)."""
+    le = topk_idx.astype(np.int64) - int(offset)
+    le = le[(le >= 0) & (le < e_local)]
+    return np.bincount(le, minlength=e_local).astype(np.int64)
+
+
+def moe_forward(logits, bias, hidden_u8, hidden_scale, get_expert, offset: int, routed_scaling_factor: float,
+                e_local: int = 32, token_subset=None, routing=None):
+    """The whole layer (ref_moe.py:5-167) on CPU.
+
+    get_expert(le) -> (w13_u8 [4096, 7168], s13 [32, 56], w2_u8 [7168, 2048], s2 [56, 16])
+    token_subset: optional token indices; only those output rows are computed
+    (each output row depends only on its own token).
+    Returns dict: out_f32 [n, 7168], out_bf16 (uint16 bits), rows, topk_idx, counts, routing.
+    """
+    r = routing if routing is not None else route(logits, bias, routed_scaling_factor)
+    topk_idx, weights = r["topk_idx"], r["weights"]
+    T = topk_idx.shape[0]
+    rows = np.arange(T) if token_subset is None else np.asarray(token_subset, dtype=np.int64)
+    pos = {int(t): i for i, t in enumerate(rows)}
+    out = np.zeros((len(rows), H), dtype=np.float32)                   # :129
+    hidden_u8 = np.asarray(hidden_u8)
+    hidden_scale = np.asarray(hidden_scale, dtype=np.float32)
+    for le in range(e_local):                                           # :134
+        ge = int(offset) + le
+        if ge < 0 or ge >= E:                                           # :136
+            continue
+        sel = (topk_idx[rows] == ge).any(axis=1)                        # :140
+        if not sel.any():                                               # :141
+            continue
+        tok = rows[sel]                                                 # :144
+        w13, s13, w2, s2 = get_expert(le)
+        A_e = dequant_rows(hidden_u8[tok], hidden_scale[:, tok])        # :69-78, :148
+        W13 = dequant_blocks(as_u8(w13), as_f32(s13))                   # :80-86
+        G1 = A_e @ W13.T                                                # :153
+        X1, X2 = G1[:, :I], G1[:, I:]                                   # :156-157
+        C = (X2 / (np.float32(1.0) + np.exp(-X2))) * X1                 # :158-159
+        W2 = dequant_blocks(as_u8(w2), as_f32(s2))                      # :88-92
+        O = C @ W2.T                                                    # :162
+        w_tok = weights[tok, ge]                                        # :165
+        idx = np.fromiter((pos[int(t)] for t in tok), dtype=np.int64, count=len(tok))
+        out[idx] += O * w_tok[:, None]                                  # :166
+    return {
+        "out_f32": out, "out_bf16": f32_to_bf16_bits(out), "rows": rows, "topk_idx": topk_idx,
+        "counts": local_counts(topk_idx, offset, e_local), "routing": r,
+    }
+
+
+# ---------------------------------------------------------------------------
+# Comparison helpers used by the tests.
+# ---------------------------------------------------------------------------
+def routing_mismatch_is_tie(routing: dict, t: int, ulps: int = 4) -> bool:
+    """True if token t's selection boundary is within ``ulps`` float32 ulps of a
+    tie: the 8th vs 9th kept score, or the 4th vs 5th group score. A routing
+    difference at such a token can come from a 1-ulp difference of exp()
+    between libraries and is reported as a tie, not a failure."""
+    sb = routing["pruned"][t]
+    srt = np.sort(sb)[::-1]
+    gs = np.sort(routing["group_scores"][t])[::-1]
+
+    def close(a, b):
+        tol = ulps * np.spacing(np.float32(max(abs(a), abs(b))))
+        return abs(float(a) - float(b)) <= tol
+
+    return close(srt[TOP_K - 1], srt[TOP_K]) or close(gs[TOPK_GROUP - 1], gs[TOPK_GROUP])
+
+
+def allclose_fraction(y: np.ndarray, y_ref: np.ndarray, atol: float = 1e-2, rtol: float = 1e-2) -> float:
+    """Fraction of elements with |y - y_ref| <= atol + rtol * |y_ref|."""
+    y = np.asarray(y, dtype=np.float32)
+    y_ref = np.asarray(y_ref, dtype=np.float32)
+    if y.size == 0:
+        return 1.0
+    return float(np.mean(np.abs(y - y_ref) <= atol + rtol * np.abs(y_ref)))
