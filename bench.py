@@ -193,6 +193,16 @@ def bench_ours(args):
     for T in Ts:
         kern[T] /= args.steps
 
+    # host-side enqueue cost of one call (argument checks, ctypes, launches)
+    host_us = {}
+    for T in Ts:
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(20):
+            call(T)
+        host_us[T] = (time.perf_counter() - t0) / 20 * 1e6
+        torch.cuda.synchronize()
+
     # end to end through the public API with host buffers (pinned), H2D of the
     # call's inputs and D2H of its output inside the events
     host_in = {T: [acts[T].logits.pin_memory(), acts[T].bias.pin_memory(),
@@ -231,7 +241,8 @@ def bench_ours(args):
         ms = per_T_ms[T]
         t_roof_ms = max(byts / (hbm_peak * 1e9), flops / (fp8_peak * 1e12)) * 1e3
         sweep[str(T)] = {
-            "us": round(ms * 1e3, 2), "e2e_us": round(e2e_ms[T] * 1e3, 2), **st,
+            "us": round(ms * 1e3, 2), "e2e_us": round(e2e_ms[T] * 1e3, 2), "host_enqueue_us": round(host_us[T], 1),
+            **st,
             "tflops": round(flops / (ms * 1e-3) / 1e12, 3), "gbs": round(byts / (ms * 1e-3) / 1e9, 1),
             "roofline_frac": round(t_roof_ms / ms, 4),
             "kernel_us": {k: round(v * 1e3, 2) for k, v in zip(

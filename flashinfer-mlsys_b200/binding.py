@@ -45,8 +45,49 @@ def _ptr(t):
     return None if t is None else t.data_ptr()
 
 
+def _chk(t, name, dtype, shape, dev):
+    """Fast-path check of one tensor (dtype, shape, device, contiguity)."""
+    if t.dtype != dtype or t.shape != shape or t.device != dev or not t.is_contiguous():
+        _tensor(t, name, dtype, shape)
+        _need(t.device == dev, f"{name} must be on {dev}")
+
+
+try:  # raw current-stream handle without constructing a Stream object
+    _raw_stream = torch._C._cuda_getCurrentRawStream
+except AttributeError:  # pragma: no cover
+    _raw_stream = None
+
+
 def _stream(device: torch.device) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(device.index)
     return torch.cuda.current_stream(device).cuda_stream
+
+
+# Weight tensors are the same objects call after call; remember the ones
+# already validated (keyed by identity and data pointer).
+_VALID_WEIGHTS: dict = {}
+
+
+def _weights_ok(w1, s1, w2, s2, e_local, dev):
+    key = (id(w1), id(s1), id(w2), id(s2))
+    sig = (w1.data_ptr(), s1.data_ptr(), w2.data_ptr(), s2.data_ptr(), e_local, dev)
+    if _VALID_WEIGHTS.get(key) == sig:
+        return
+    _check_weights(w1, s1, w2, s2, e_local)
+    for t in (w1, s1, w2, s2):
+        _need(t.device == dev, "all tensors must be on the same device")
+    if len(_VALID_WEIGHTS) > 64:
+        _VALID_WEIGHTS.clear()
+    _VALID_WEIGHTS[key] = sig
+
+
+def _call(dev, fn, *args):
+    """Run a C-ABI call with `dev` current (no device switch in the common case)."""
+    if dev.index == torch.cuda.current_device():
+        return fn(*args)
+    with torch.cuda.device(dev):
+        return fn(*args)
 
 
 def _check_weights(w1, s1, w2, s2, e_local):
@@ -74,36 +115,35 @@ def kernel_ex(
 ) -> None:
     """``kernel`` plus optional device outputs of this call's routing decision
     (int32 [T, 8] ids, f32 [T, 8] weights, int32 [E_local] per-expert counts)."""
-    _need(routing_logits.dim() == 2, "routing_logits must be 2-D [seq_len, 256]")
+    if routing_logits.dim() != 2:
+        raise ValueError("routing_logits must be 2-D [seq_len, 256]")
     T = routing_logits.shape[0]
     e_local = gemm1_weights.shape[0]
-    _tensor(routing_logits, "routing_logits", torch.float32, (T, NUM_EXPERTS))
-    _tensor(routing_bias, "routing_bias", torch.bfloat16, (NUM_EXPERTS,))
-    _tensor(hidden_states, "hidden_states", _E4M3, (T, HIDDEN_SIZE))
-    _tensor(hidden_states_scale, "hidden_states_scale", torch.float32, (HIDDEN_SIZE // BLOCK_Q, T))
-    _check_weights(gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, e_local)
-    _tensor(output, "output", torch.bfloat16, (T, HIDDEN_SIZE))
-    if topk_ids is not None:
-        _tensor(topk_ids, "topk_ids", torch.int32, (T, TOP_K))
-    if topk_weights is not None:
-        _tensor(topk_weights, "topk_weights", torch.float32, (T, TOP_K))
-    if expert_counts is not None:
-        _tensor(expert_counts, "expert_counts", torch.int32, (e_local,))
     dev = hidden_states.device
-    for t in (routing_logits, routing_bias, hidden_states_scale, gemm1_weights, gemm2_weights, output):
-        _need(t.device == dev, "all tensors must be on the same device")
+    _need(dev.type == "cuda", "hidden_states must be a CUDA tensor")
+    _chk(routing_logits, "routing_logits", torch.float32, (T, NUM_EXPERTS), dev)
+    _chk(routing_bias, "routing_bias", torch.bfloat16, (NUM_EXPERTS,), dev)
+    _chk(hidden_states, "hidden_states", _E4M3, (T, HIDDEN_SIZE), dev)
+    _chk(hidden_states_scale, "hidden_states_scale", torch.float32, (HIDDEN_SIZE // BLOCK_Q, T), dev)
+    _chk(output, "output", torch.bfloat16, (T, HIDDEN_SIZE), dev)
+    _weights_ok(gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, e_local, dev)
+    if topk_ids is not None:
+        _chk(topk_ids, "topk_ids", torch.int32, (T, TOP_K), dev)
+    if topk_weights is not None:
+        _chk(topk_weights, "topk_weights", torch.float32, (T, TOP_K), dev)
+    if expert_counts is not None:
+        _chk(expert_counts, "expert_counts", torch.int32, (e_local,), dev)
     lib = _lib.load()
-    with torch.cuda.device(dev):
-        rc = lib.moe_fp8_ds_kernel_ex(
-            routing_logits.data_ptr(), routing_bias.data_ptr(), hidden_states.data_ptr(),
-            hidden_states_scale.data_ptr(), gemm1_weights.data_ptr(), gemm1_weights_scale.data_ptr(),
-            gemm2_weights.data_ptr(), gemm2_weights_scale.data_ptr(), int(local_expert_offset),
-            float(routed_scaling_factor), output.data_ptr(), T, e_local,
-            _ptr(topk_ids), _ptr(topk_weights), _ptr(expert_counts), _stream(dev))
-    _lib.check(rc, "moe_fp8_ds_kernel_ex")
+    rc = _call(dev, lib.moe_fp8_ds_kernel_ex,
+               routing_logits.data_ptr(), routing_bias.data_ptr(), hidden_states.data_ptr(),
+               hidden_states_scale.data_ptr(), gemm1_weights.data_ptr(), gemm1_weights_scale.data_ptr(),
+               gemm2_weights.data_ptr(), gemm2_weights_scale.data_ptr(), int(local_expert_offset),
+               float(routed_scaling_factor), output.data_ptr(), T, e_local,
+               _ptr(topk_ids), _ptr(topk_weights), _ptr(expert_counts), _stream(dev))
+    if rc:
+        _lib.check(rc, "moe_fp8_ds_kernel_ex")
 
 
-@torch.no_grad()
 def kernel(
     routing_logits: torch.Tensor,
     routing_bias: torch.Tensor,

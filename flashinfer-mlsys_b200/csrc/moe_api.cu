@@ -33,7 +33,34 @@ EncodeTiledFn encode_fn() {
 
 // 2D byte matrix [rows][cols] (row stride = cols bytes), 128x128 box,
 // 128-byte swizzle (matches the UMMA K-major SWIZZLE_128B operand layout).
+// Encoded maps are cached by (base, cols, rows): a map holds no state beyond
+// those, and callers typically reuse their weight and workspace buffers.
+struct MapKey {
+  const void* base;
+  uint64_t cols, rows;
+};
+constexpr int kMapCache = 32;
+MapKey g_map_key[kMapCache];
+CUtensorMap g_map_val[kMapCache];
+int g_map_next = 0;
+
+bool encode_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows);
+
 bool make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows) {
+  for (int i = 0; i < kMapCache; ++i) {
+    if (g_map_key[i].base == base && g_map_key[i].cols == cols && g_map_key[i].rows == rows && base) {
+      *m = g_map_val[i];
+      return true;
+    }
+  }
+  if (!encode_map(m, base, cols, rows)) return false;
+  g_map_key[g_map_next] = MapKey{base, cols, rows};
+  g_map_val[g_map_next] = *m;
+  g_map_next = (g_map_next + 1) % kMapCache;
+  return true;
+}
+
+bool encode_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {cols, rows};
@@ -90,6 +117,14 @@ size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_
   return off;
 }
 
+void forget_maps(const void* base, size_t bytes) {
+  const uint8_t* b = static_cast<const uint8_t*>(base);
+  for (int i = 0; i < kMapCache; ++i) {
+    const uint8_t* k = static_cast<const uint8_t*>(g_map_key[i].base);
+    if (k >= b && k < b + bytes) g_map_key[i] = MapKey{nullptr, 0, 0};
+  }
+}
+
 int get_workspace(int64_t T, int e_local, Workspace** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MOE_ERR_CUDA;
@@ -102,6 +137,7 @@ int get_workspace(int64_t T, int e_local, Workspace** out) {
   if (w.base && w.e_local == e_local && w.t_cap > t_new) t_new = w.t_cap;
   if (w.base) {
     cudaDeviceSynchronize();
+    forget_maps(w.base, w.bytes);
     cudaFree(w.base);
     w = Workspace{};
   }
@@ -126,12 +162,16 @@ int get_workspace(int64_t T, int e_local, Workspace** out) {
 }
 
 int check_device() {
+  static int major_cache[64] = {0};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return MOE_ERR_NO_DEVICE;
-  int major = 0;
-  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
-    return MOE_ERR_NO_DEVICE;
-  return major == 10 ? MOE_OK : MOE_ERR_NO_DEVICE;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MOE_ERR_NO_DEVICE;
+  if (!major_cache[dev]) {
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+      return MOE_ERR_NO_DEVICE;
+    major_cache[dev] = major;
+  }
+  return major_cache[dev] == 10 ? MOE_OK : MOE_ERR_NO_DEVICE;
 }
 
 // Optional per-kernel CUDA events (moe_fp8_ds_profile_enable).
@@ -156,6 +196,7 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
                  int32_t* user_ids, float* user_w, int32_t* user_counts, void* stream, bool route_only) {
   if (T < 0 || T > (int64_t(1) << 24) || !valid_e_local(E_l)) return MOE_ERR_INVALID_ARG;
   if (offset < -(int64_t(1) << 30) || offset > (int64_t(1) << 30)) return MOE_ERR_INVALID_ARG;
+  if (T == 0) return check_device();  // empty tensors may carry null data pointers
   if (logits) {
     if (!bias) return MOE_ERR_INVALID_ARG;
     if (!aligned16(logits) || !aligned16(bias)) return MOE_ERR_ALIGNMENT;
@@ -169,7 +210,6 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
   int rc = check_device();
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (T == 0) return MOE_OK;
 
   std::lock_guard<std::mutex> lk(g_mu);
   Workspace* ws = nullptr;
@@ -230,7 +270,7 @@ int moe_fp8_ds_kernel_ex(const float* routing_logits, const void* routing_bias, 
                          double routed_scaling_factor, void* output, int64_t seq_len, int64_t num_local_experts,
                          int32_t* topk_ids_out, float* topk_weights_out, int32_t* expert_counts_out,
                          void* stream) {
-  if (!routing_logits) return MOE_ERR_INVALID_ARG;
+  if (!routing_logits && seq_len != 0) return MOE_ERR_INVALID_ARG;
   return run_pipeline(routing_logits, routing_bias, nullptr, nullptr, hidden_states, hidden_states_scale,
                       gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
                       routed_scaling_factor, output, 0, seq_len, num_local_experts, topk_ids_out, topk_weights_out,
@@ -251,7 +291,7 @@ int moe_fp8_ds_kernel(const float* routing_logits, const void* routing_bias, con
 int moe_fp8_ds_route(const float* routing_logits, const void* routing_bias, int64_t seq_len,
                      int64_t local_expert_offset, int64_t num_local_experts, double routed_scaling_factor,
                      int32_t* topk_ids_out, float* topk_weights_out, int32_t* expert_counts_out, void* stream) {
-  if (!routing_logits || !topk_ids_out || !topk_weights_out) return MOE_ERR_INVALID_ARG;
+  if (seq_len != 0 && (!routing_logits || !topk_ids_out || !topk_weights_out)) return MOE_ERR_INVALID_ARG;
   return run_pipeline(routing_logits, routing_bias, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
                       nullptr, local_expert_offset, routed_scaling_factor, nullptr, 0, seq_len, num_local_experts,
                       topk_ids_out, topk_weights_out, expert_counts_out, stream, true);
@@ -261,7 +301,7 @@ int moe_fp8_ds_experts(const void* hidden_states, const float* hidden_states_sca
                        const float* topk_weights, const void* gemm1_weights, const float* gemm1_weights_scale,
                        const void* gemm2_weights, const float* gemm2_weights_scale, int64_t local_expert_offset,
                        int64_t num_rows, int64_t num_local_experts, void* output, int output_fp32, void* stream) {
-  if (!topk_ids || !topk_weights) return MOE_ERR_INVALID_ARG;
+  if (num_rows != 0 && (!topk_ids || !topk_weights)) return MOE_ERR_INVALID_ARG;
   return run_pipeline(nullptr, nullptr, topk_ids, topk_weights, hidden_states, hidden_states_scale, gemm1_weights,
                       gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset, 1.0, output,
                       output_fp32 ? 1 : 0, num_rows, num_local_experts, nullptr, nullptr, nullptr, stream, false);
@@ -310,6 +350,7 @@ int moe_fp8_ds_release_workspace(void) {
   auto it = g_ws.find(dev);
   if (it != g_ws.end() && it->second.base) {
     cudaDeviceSynchronize();
+    forget_maps(it->second.base, it->second.bytes);
     cudaFree(it->second.base);
     g_ws.erase(it);
   }

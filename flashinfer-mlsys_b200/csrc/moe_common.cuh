@@ -49,10 +49,12 @@ constexpr int kStageA = kTileM * kBlk;        // 16 KB of e4m3
 constexpr int kStageB = kTileN * kBlk;        // 32 KB of e4m3
 constexpr int kStageBytes = kStageA + kStageB;
 
-constexpr int kGemmThreads = 576;             // 18 warps
-constexpr int kEpiWarp0 = 2;                  // warps 2..17 run the epilogue
+constexpr int kGemmThreads = 608;             // 19 warps
+constexpr int kScaleWarp = 2;                 // warp 2 streams block scales into shared memory
+constexpr int kEpiWarp0 = 3;                  // warps 3..18 run the epilogue
 constexpr int kEpiWarps = 16;
 constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kScaleSlots = 8;                // depth of the scale ring (K blocks ahead)
 
 // Split-K of GEMM1 reduces fp32 partial tiles in a bounded scratch area.
 constexpr int kMaxSplitMTiles = 32;
@@ -215,6 +217,31 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
 // N >> 3 in [17,23), M >> 4 in [24,29).
 __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
   return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// ---- cp.async (per-thread asynchronous global -> shared copies) ------------
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+// Arrive on `bar` once this thread's earlier cp.async copies have landed
+// (the barrier's expected count includes this arrival).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// ---- programmatic dependent launch ---------------------------------------
+// Kernels after the first of a call are launched with programmatic stream
+// serialisation: they may start while the previous kernel drains, run their
+// prologue, and block in griddep_wait() until it has completed and its memory
+// is visible. Each kernel releases its dependent only after its own wait, so
+// the kernel two steps back has always completed when a kernel starts.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ---- misc -----------------------------------------------------------------

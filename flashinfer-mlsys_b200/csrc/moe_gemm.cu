@@ -16,7 +16,10 @@
 //   warp 1      TMEM owner + MMA issuer (one lane): 4 x tcgen05.mma
 //               (M128 N256 K32, e4m3 x e4m3 -> f32) per K block into one of
 //               two 256-column TMEM partial accumulators.
-//   warps 2-17  epilogue: per K block, read the fresh partial from TMEM and
+//   warp 2      scale loader: cp.async copies of the 128 row scales and the
+//               weight-block scales of every K block into an 8-deep shared
+//               ring, running ahead of the epilogue.
+//   warps 3-18  epilogue: per K block, read the fresh partial from TMEM and
 //               promote it in fp32 registers with a_scale[row,kb] *
 //               w_scale[nblk,kb] (the block scales are arbitrary fp32, so no
 //               hardware block-scale mode applies); after the last K block
@@ -74,7 +77,15 @@ __device__ __forceinline__ Unit decode_unit(int u, int split, const int* prefix,
   return x;
 }
 
-struct __align__(8) SmemCtl {
+struct __align__(16) ScaleSlot {
+  float a[kTileM];  // a_scale of the 128 rows of the m-tile for this K block
+  float w[4];       // weight-block scales: GEMM1 {gate, up}; GEMM2 {slab 0, slab 1}
+};
+
+struct __align__(16) SmemCtl {
+  ScaleSlot scales[kScaleSlots];
+  uint64_t sfull[kScaleSlots];
+  uint64_t sempty[kScaleSlots];
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t tfull[2];
@@ -188,6 +199,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&ctl->tfull[b], 1);
       mbar_init(&ctl->tempty[b], kEpiWarps);
     }
+    for (int j = 0; j < kScaleSlots; ++j) {
+      mbar_init(&ctl->sfull[j], 32);
+      mbar_init(&ctl->sempty[j], kEpiWarps);
+    }
     mbar_init(&ctl->mma_done, 1);
     mbar_init(&ctl->epi_bar, kEpiWarps);
     ctl->abort_flag = 0;
@@ -195,12 +210,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tensormap(&map_a);
     prefetch_tensormap(&map_w);
   }
-  for (int e = tid; e <= E_l; e += blockDim.x) ctl->prefix[e] = p.plan->mtile_prefix[e];
-  for (int e = tid; e < E_l; e += blockDim.x) ctl->count[e] = p.plan->count[e];
   if (warp == 1) {
     tmem_alloc(&ctl->tmem_base, 512);
     tmem_relinquish();
   }
+  // everything above overlaps the previous kernel's tail; from here on we
+  // read what it produced
+  griddep_wait();
+  griddep_launch_dependents();
+  for (int e = tid; e <= E_l; e += blockDim.x) ctl->prefix[e] = p.plan->mtile_prefix[e];
+  for (int e = tid; e < E_l; e += blockDim.x) ctl->count[e] = p.plan->count[e];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -283,6 +302,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         mbar_wait_bounded(&ctl->mma_done, 0, kWaitLimitNs);
       }
     }
+  } else if (warp == kScaleWarp) {
+    // ======================= scale loader =======================
+    uint32_t it = 0;
+    for (int u = blockIdx.x; u < units && !aborted(ctl); u += gridDim.x) {
+      const Unit x = decode_unit<kMode>(u, split, ctl->prefix, ctl->count, E_l);
+      bool ok = true;
+      for (int kb = x.kb0; kb < x.kb1; ++kb, ++it) {
+        const int j = it % kScaleSlots;
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&ctl->sempty[j], ((it / kScaleSlots) & 1u) ^ 1u,
+                                                       kWaitLimitNs));
+        if (!ok) {
+          signal_abort(ctl, p.status);
+          break;
+        }
+        ScaleSlot* sl = &ctl->scales[j];
+        const int ka = (kMode == 1) ? kb : (kb % kInterBlocks);
+        cp_async_16(&sl->a[4 * lane], p.a_scale + (size_t)ka * p.rows_cap + (size_t)x.gm * kTileM + 4 * lane);
+        if (lane < 2) {
+          const float* src;
+          if (kMode == 1)
+            src = p.w_scale + ((size_t)x.e * kGemm1NBlocks + lane * kNT1 + x.n) * kHiddenBlocks + kb;
+          else
+            src = p.w_scale + ((size_t)x.e * kHiddenBlocks + 2 * x.n + lane) * kInterBlocks + ka;
+          cp_async_4(&sl->w[lane], src);
+        }
+        cp_async_arrive_noinc(&ctl->sfull[j]);
+      }
+      if (!ok) break;
+    }
+    cp_async_wait_all();
   } else {
     // ======================= epilogue (16 warps) =======================
     const int q = warp & 3;              // TMEM lane quarter accessible to this warp
@@ -302,19 +351,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       for (int kb = x.kb0; kb < x.kb1; ++kb, ++gkb) {
         const uint32_t buf = gkb & 1u;
-        float f0, f1;
-        if (kMode == 1) {
-          const float as = __ldg(p.a_scale + (size_t)kb * p.rows_cap + row);
-          const float* ws = p.w_scale + (size_t)x.e * (kGemm1NBlocks * kHiddenBlocks);
-          f0 = as * __ldg(ws + x.n * kHiddenBlocks + kb);
-          f1 = as * __ldg(ws + (kNT1 + x.n) * kHiddenBlocks + kb);
-        } else {
-          const int kr = kb % kInterBlocks;
-          float as = __ldg(p.a_scale + (size_t)kr * p.rows_cap + row);
-          if (kb >= kInterBlocks) as *= kLoScale;
-          const int nb = 2 * x.n + (cg >> 1);
-          f0 = f1 = as * __ldg(p.w_scale + ((size_t)x.e * kHiddenBlocks + nb) * kInterBlocks + kr);
+        const int j = gkb % kScaleSlots;
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&ctl->sfull[j], (gkb / kScaleSlots) & 1u, kWaitLimitNs))) {
+          signal_abort(ctl, p.status);
+          ok = false;
+          break;
         }
+        float f0, f1;
+        {
+          const ScaleSlot* sl = &ctl->scales[j];
+          const float as = sl->a[row_in_tile];
+          if (kMode == 1) {
+            f0 = as * sl->w[0];
+            f1 = as * sl->w[1];
+          } else {
+            f0 = f1 = as * ((kb >= kInterBlocks) ? kLoScale : 1.0f) * sl->w[cg >> 1];
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->sempty[j]);
         const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(&ctl->tfull[buf], (gkb >> 1) & 1u, kWaitLimitNs));
         if (!got) {
           signal_abort(ctl, p.status);
@@ -418,9 +473,7 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
     if (e != cudaSuccess) return e;
     configured[kMode - 1] = 1;
   }
-  int dev = 0, sms = kSMs;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = device_sm_count();
   GemmArgs p{};
   p.plan = ws.plan;
   p.a_scale = (kMode == 1) ? ws.a1_scale : ws.inter_scale;
@@ -435,8 +488,7 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
   p.row_weight = ws.row_weight;
   p.accum = ws.accum;
   p.status = ws.status;
-  moe_gemm_kernel<kMode><<<sms, kGemmThreads, smem, s>>>(map_a, map_w, p);
-  return cudaGetLastError();
+  return launch_k(moe_gemm_kernel<kMode>, dim3(sms), dim3(kGemmThreads), smem, s, true, map_a, map_w, p);
 }
 
 }  // namespace

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "moe_common.cuh"
 
 namespace moe {
@@ -59,7 +61,27 @@ struct PermuteArgs {
   int tokens_per_cta;
 };
 
+// Launch `kernel` on `s`; with `pdl` the launch may overlap the tail of the
+// previous kernel on the stream (the kernel must call griddep_wait() before
+// touching that kernel's outputs).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 int route_ctas_for(int T);
+int device_sm_count();  // cached per device
 int tokens_per_cta_for(int T);
 
 cudaError_t launch_route(const Workspace& ws, const RouteArgs& a, cudaStream_t s);

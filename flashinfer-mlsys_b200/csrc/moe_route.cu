@@ -17,15 +17,19 @@ namespace {
 
 constexpr int kRouteThreads = 256;  // 8 warps, one token per warp at a time
 
-struct Cand {
-  float v;   // sb (selection key)
-  float s;   // un-biased sigmoid (weight numerator)
-  int idx;   // global expert id
-};
-
-// a beats b: larger key, ties to the smaller expert id.
-__device__ __forceinline__ bool beats(float av, int ai, float bv, int bi) {
-  return av > bv || (av == bv && ai < bi);
+// Sort 8 composite keys descending (19-comparator network, all-0/1-input verified).
+__device__ __forceinline__ void cmpswap(uint64_t& a, uint64_t& b) {
+  const uint64_t hi = a > b ? a : b, lo = a > b ? b : a;
+  a = hi;
+  b = lo;
+}
+__device__ __forceinline__ void sort8_desc(uint64_t (&c)[8]) {
+  cmpswap(c[0], c[2]); cmpswap(c[1], c[3]); cmpswap(c[4], c[6]); cmpswap(c[5], c[7]);
+  cmpswap(c[0], c[4]); cmpswap(c[1], c[5]); cmpswap(c[2], c[6]); cmpswap(c[3], c[7]);
+  cmpswap(c[0], c[1]); cmpswap(c[2], c[3]); cmpswap(c[4], c[5]); cmpswap(c[6], c[7]);
+  cmpswap(c[2], c[4]); cmpswap(c[3], c[5]);
+  cmpswap(c[1], c[4]); cmpswap(c[3], c[6]);
+  cmpswap(c[1], c[2]); cmpswap(c[3], c[4]); cmpswap(c[5], c[6]);
 }
 
 __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, Workspace ws) {
@@ -34,6 +38,9 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int E_l = a.e_local;
+  // first kernel of a call: launched with normal stream ordering; let the
+  // permutation kernel get scheduled early (it waits for this grid).
+  griddep_launch_dependents();
   for (int e = tid; e < E_l; e += blockDim.x) hist[e] = 0;
   __syncthreads();
 
@@ -81,34 +88,45 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
         rank += (o > gscore || (o == gscore && gg < g)) ? 1 : 0;
       }
       const bool kept = rank < kTopKGroups;
-      float key[8];
+      // ---- top-8 of the kept candidates, ordered by (sb desc, expert id asc) ----
+      // composite key: order-preserving bits of sb in the high word, 0xFFFF - id
+      // in the low word; 0 marks a candidate of a dropped group.
+      uint64_t c[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) key[i] = kept ? sb[i] : -INFINITY;
-      // ---- 8 rounds of warp arg-max over the kept candidates ----
-      float ssum = 0.f;
-      float sel_s = 0.f;
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t u = __float_as_uint(sb[i]);
+        const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+        c[i] = kept ? ((static_cast<uint64_t>(ord) << 32) | static_cast<uint32_t>(0xFFFF - (lane * 8 + i))) : 0ull;
+      }
+      sort8_desc(c);
+      // 8 rounds: warp max of the lane heads (key word, then id word), the
+      // winning lane pops its head.
+      int sel = 0;
 #pragma unroll 1
       for (int k = 0; k < kTopK; ++k) {
-        Cand c{-INFINITY, 0.f, 0x7fffffff};
+        const uint32_t hk = static_cast<uint32_t>(c[0] >> 32);
+        const uint32_t mk = __reduce_max_sync(0xffffffffu, hk);
+        const uint32_t lo = (hk == mk) ? static_cast<uint32_t>(c[0]) : 0u;
+        const uint32_t ml = __reduce_max_sync(0xffffffffu, lo);
+        const bool win = (hk == mk) && (lo == ml);
+        if (lane == k) sel = 0xFFFF - static_cast<int>(ml);
+        if (win) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          if (beats(key[i], lane * 8 + i, c.v, c.idx)) { c.v = key[i]; c.s = s[i]; c.idx = lane * 8 + i; }
+          for (int i = 0; i < 7; ++i) c[i] = c[i + 1];
+          c[7] = 0ull;
         }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-          float ov = __shfl_xor_sync(0xffffffffu, c.v, off);
-          float os = __shfl_xor_sync(0xffffffffu, c.s, off);
-          int oi = __shfl_xor_sync(0xffffffffu, c.idx, off);
-          if (beats(ov, oi, c.v, c.idx)) { c.v = ov; c.s = os; c.idx = oi; }
-        }
-        if ((c.idx >> 3) == lane) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            if (i == (c.idx & 7)) key[i] = -INFINITY;
-        }
-        if (lane == k) { my_id = c.idx; sel_s = c.s; }
-        ssum += c.s;
       }
+      // weight numerators: recompute the un-biased sigmoid of the chosen expert
+      // (same instruction sequence as above, so the value is identical)
+      float sel_s = 0.f;
+      if (lane < kTopK) {
+        const float xl = __ldg(a.logits + (size_t)t * kExperts + sel);
+        sel_s = 1.0f / (1.0f + expf(-xl));
+        my_id = sel;
+      }
+      float ssum = sel_s;
+#pragma unroll
+      for (int off = 4; off >= 1; off >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, off);
       my_w = (sel_s / (ssum + 1e-20f)) * a.scale;
     } else if (lane < kTopK) {
       my_id = __ldg(a.given_ids + (size_t)t * kTopK + lane);
@@ -141,44 +159,60 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
 
   // ---- last CTA: per-expert counts, m-tile prefix, K-split plan ----
   __threadfence();
-  __shared__ int mt[kExperts + 1];
-  for (int e = tid; e < kExperts; e += blockDim.x) {
-    int c = 0;
-    if (e < E_l) {
-      c = atomicExch(&ws.expert_fill[e], 0);  // read and reset for the next call
-      ws.plan->count[e] = c;
-      if (a.user_counts) a.user_counts[e] = c;
-    }
-    hist[e] = c;
-    mt[e] = (c + kTileM - 1) / kTileM;
+  __shared__ int warp_tot[2][kRouteThreads / 32];
+  int c = 0;
+  if (tid < E_l) {
+    c = atomicExch(&ws.expert_fill[tid], 0);  // read and reset for the next call
+    ws.plan->count[tid] = c;
+    if (a.user_counts) a.user_counts[tid] = c;
   }
+  int m = (c + kTileM - 1) / kTileM;
+  // block-wide exclusive scan of m-tiles and total of rows over the experts
+  int incl = m, csum = c;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += y;
+    csum += __shfl_xor_sync(0xffffffffu, csum, off);
+  }
+  if (lane == 31) warp_tot[0][warp] = incl;
+  if (lane == 0) warp_tot[1][warp] = csum;
   __syncthreads();
-  if (tid == 0) {
-    int run = 0, nas = 0;
-    for (int e = 0; e < E_l; ++e) {
-      ws.plan->mtile_prefix[e] = run;
-      run += mt[e];
-      nas += hist[e];
-    }
-    ws.plan->mtile_prefix[E_l] = run;
-    ws.plan->total_mtiles = run;
-    ws.plan->n_assign = nas;
-    // K split: minimise waves * (k-blocks per unit + per-unit overhead).
-    auto pick = [&](int tiles, int nkb, int smax) {
-      if (tiles <= 0) return 1;
-      int best = 1;
-      long best_cost = 0x7fffffffffffL;
-      for (int sp = 1; sp <= smax; ++sp) {
-        long units = (long)tiles * sp;
-        long waves = (units + kSMs - 1) / kSMs;
-        long cost = waves * ((nkb + sp - 1) / sp + 3);
-        if (cost < best_cost) { best_cost = cost; best = sp; }
-      }
-      return best;
+  int base = 0, total = 0, nas = 0;
+  for (int w = 0; w < kRouteThreads / 32; ++w) {
+    if (w < warp) base += warp_tot[0][w];
+    total += warp_tot[0][w];
+    nas += warp_tot[1][w];
+  }
+  if (tid < E_l) ws.plan->mtile_prefix[tid] = base + incl - m;
+  if (warp == 0) {
+    // K split: minimise waves * (K blocks per unit + per-unit overhead); lane = split - 1
+    auto cost = [&](int tiles, int nkb, int smax, int sp) -> long long {
+      if (sp > smax || tiles <= 0) return 0x7fffffffffffLL;
+      const long long units = (long long)tiles * sp;
+      return ((units + kSMs - 1) / kSMs) * ((nkb + sp - 1) / sp + 3);
     };
-    ws.plan->split1 = (run <= kMaxSplitMTiles) ? pick(run * kNT1, kKB1, 14) : 1;
-    ws.plan->split2 = pick(run * kNT2, kKB2, 8);
-    *ws.done_ctas = 0u;
+    const int sp = lane + 1;
+    const long long c1 = (total <= kMaxSplitMTiles) ? cost(total * kNT1, kKB1, 14, sp) : (sp == 1 ? 0 : 0x7fffffffffffLL);
+    const long long c2 = cost(total * kNT2, kKB2, 8, sp);
+    // pack (cost, split) so that the minimum prefers the smaller split on ties
+    unsigned long long k1 = (static_cast<unsigned long long>(c1) << 8) | sp;
+    unsigned long long k2 = (static_cast<unsigned long long>(c2) << 8) | sp;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      const unsigned long long o1 = __shfl_xor_sync(0xffffffffu, k1, off);
+      const unsigned long long o2 = __shfl_xor_sync(0xffffffffu, k2, off);
+      k1 = o1 < k1 ? o1 : k1;
+      k2 = o2 < k2 ? o2 : k2;
+    }
+    if (lane == 0) {
+      ws.plan->mtile_prefix[E_l] = total;
+      ws.plan->total_mtiles = total;
+      ws.plan->n_assign = nas;
+      ws.plan->split1 = total > 0 ? static_cast<int>(k1 & 0xFF) : 1;
+      ws.plan->split2 = total > 0 ? static_cast<int>(k2 & 0xFF) : 1;
+      *ws.done_ctas = 0u;
+    }
   }
 }
 
@@ -187,6 +221,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
 __global__ void __launch_bounds__(256) permute_kernel(PermuteArgs a, Workspace ws) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + warp;
+  griddep_wait();
+  griddep_launch_dependents();
   if (t >= a.T) return;
   const int E_l = ws.e_local;
   int row = -1;
@@ -230,6 +266,7 @@ __global__ void __launch_bounds__(256) permute_kernel(PermuteArgs a, Workspace w
 // out = cast(accum); accum = 0. Eight elements per thread.
 __global__ void __launch_bounds__(256) finalize_kernel(float* __restrict__ accum, void* __restrict__ out,
                                                        int64_t n8, int out_fp32) {
+  griddep_wait();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
     float4* p = reinterpret_cast<float4*>(accum) + 2 * i;
     float4 x0 = p[0], x1 = p[1];
@@ -256,6 +293,18 @@ __global__ void __launch_bounds__(256) finalize_kernel(float* __restrict__ accum
 
 }  // namespace
 
+int device_sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kSMs;
+  if (!cache[dev]) {
+    int n = kSMs;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
 int tokens_per_cta_for(int T) {
   // one token per warp for small T; at most ~kSMs routing CTAs for large T
   int per = (T + kSMs - 1) / kSMs;
@@ -271,14 +320,12 @@ int route_ctas_for(int T) {
 
 cudaError_t launch_route(const Workspace& ws, const RouteArgs& a, cudaStream_t s) {
   const int grid = route_ctas_for(a.T);
-  route_plan_kernel<<<grid, kRouteThreads, 0, s>>>(a, ws);
-  return cudaGetLastError();
+  return launch_k(route_plan_kernel, dim3(grid), dim3(kRouteThreads), 0, s, false, a, ws);
 }
 
 cudaError_t launch_permute(const Workspace& ws, const PermuteArgs& a, cudaStream_t s) {
   if (a.T <= 0) return cudaSuccess;
-  permute_kernel<<<(a.T + 7) / 8, 256, 0, s>>>(a, ws);
-  return cudaGetLastError();
+  return launch_k(permute_kernel, dim3((a.T + 7) / 8), dim3(256), 0, s, true, a, ws);
 }
 
 cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32, cudaStream_t s) {
@@ -286,8 +333,7 @@ cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32,
   if (n8 == 0) return cudaSuccess;
   int64_t blocks = (n8 + 255) / 256;
   if (blocks > 8 * kSMs) blocks = 8 * kSMs;
-  finalize_kernel<<<(int)blocks, 256, 0, s>>>(ws.accum, out, n8, out_fp32);
-  return cudaGetLastError();
+  return launch_k(finalize_kernel, dim3((unsigned)blocks), dim3(256), 0, s, true, ws.accum, out, n8, out_fp32);
 }
 
 }  // namespace moe
