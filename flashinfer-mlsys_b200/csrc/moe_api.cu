@@ -96,9 +96,12 @@ size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_
   w.done_ctas = reinterpret_cast<uint32_t*>(take(4));
   w.status = reinterpret_cast<unsigned*>(take(4));
   w.tile_sem = reinterpret_cast<int32_t*>(take((size_t)kMaxSplitMTiles * kNT1 * 4));
-  w.accum = reinterpret_cast<float*>(take(Tz * kHidden * 4));
+  w.tile_sem2 = reinterpret_cast<int32_t*>(take((size_t)kMaxSplitMTiles * kNT2 * 4));
   w.g_part = reinterpret_cast<float*>(take((size_t)kMaxSplitMTiles * kTileM * kGemm1N * 4));
+  w.g2_part = reinterpret_cast<float*>(take((size_t)kMaxSplitMTiles * kTileM * kHidden * 4));
   if (zero_bytes) *zero_bytes = off;
+  w.token_rows = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
+  w.out_rows = reinterpret_cast<float*>(take((size_t)rows * kHidden * 4));
   w.plan = reinterpret_cast<Plan*>(take(sizeof(Plan)));
   w.topk_ids = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
   w.topk_w = reinterpret_cast<float*>(take(Tz * kTopK * 4));

@@ -42,9 +42,10 @@ struct GemmArgs {
   float* inter_scale;       // GEMM1 out: [16][rows_cap]
   float* g_part;            // GEMM1 split-K scratch: [kMaxSplitMTiles*128][4096]
   int32_t* tile_sem;        // GEMM1 split-K counters: [kMaxSplitMTiles][16]
-  const int32_t* row_token; // GEMM2
-  const float* row_weight;  // GEMM2
-  float* accum;             // GEMM2 out: [T][7168]
+  const float* row_weight;  // GEMM2: routing weight of each permuted row
+  float* out_rows;          // GEMM2 out: [rows_cap][7168] weighted expert outputs
+  float* g2_part;           // GEMM2 split-K scratch: [kMaxSplitMTiles*128][7168]
+  int32_t* tile_sem2;       // GEMM2 split-K counters: [kMaxSplitMTiles][28]
   unsigned* status;
 };
 
@@ -439,13 +440,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       } else {
-        if (valid) {
-          const int tok = __ldg(p.row_token + row);
-          const float w = __ldg(p.row_weight + row);
-          float* dst = p.accum + (size_t)tok * kHidden + x.n * kTileN + cg * 64;
+        const float w = valid ? __ldg(p.row_weight + row) : 0.f;
+        float4* dst = reinterpret_cast<float4*>(p.out_rows + row * kHidden + x.n * kTileN + cg * 64);
+        if (split == 1) {
+          if (valid) {
 #pragma unroll
-          for (int i = 0; i < 64; i += 4)
-            red_add_v4(dst + i, w * acc[i], w * acc[i + 1], w * acc[i + 2], w * acc[i + 3]);
+            for (int i = 0; i < 16; ++i)
+              dst[i] = make_float4(w * acc[4 * i], w * acc[4 * i + 1], w * acc[4 * i + 2], w * acc[4 * i + 3]);
+          }
+        } else {
+          // split-K: partial sums meet in fp32 scratch; the last arriving CTA
+          // of this (m-tile, n-tile) writes the finished rows.
+          float* g = p.g2_part + row * kHidden + x.n * kTileN + cg * 64;
+          if (valid) {
+#pragma unroll
+            for (int i = 0; i < 64; i += 4)
+              red_add_v4(g + i, w * acc[i], w * acc[i + 1], w * acc[i + 2], w * acc[i + 3]);
+          }
+          __threadfence();
+          if (!es.sync(ctl, p.status)) break;
+          if (warp == kEpiWarp0 && lane == 0) {
+            const int old = atomicAdd(&p.tile_sem2[x.gm * kNT2 + x.n], 1);
+            ctl->fixup_flag = (old == split - 1) ? 1 : 0;
+          }
+          if (!es.sync(ctl, p.status)) break;
+          if (ctl->fixup_flag) {
+            __threadfence();
+            if (valid) {
+              float4* pg = reinterpret_cast<float4*>(g);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                dst[i] = __ldcg(pg + i);
+                __stcg(pg + i, make_float4(0.f, 0.f, 0.f, 0.f));
+              }
+            }
+            if (warp == kEpiWarp0 && lane == 0) p.tile_sem2[x.gm * kNT2 + x.n] = 0;
+          }
         }
       }
     }
@@ -484,9 +514,10 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
   p.inter_scale = ws.inter_scale;
   p.g_part = ws.g_part;
   p.tile_sem = ws.tile_sem;
-  p.row_token = ws.row_token;
   p.row_weight = ws.row_weight;
-  p.accum = ws.accum;
+  p.out_rows = ws.out_rows;
+  p.g2_part = ws.g2_part;
+  p.tile_sem2 = ws.tile_sem2;
   p.status = ws.status;
   return launch_k(moe_gemm_kernel<kMode>, dim3(sms), dim3(kGemmThreads), smem, s, true, map_a, map_w, p);
 }

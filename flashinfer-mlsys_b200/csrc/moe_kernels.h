@@ -30,9 +30,12 @@ struct Workspace {
   float* row_weight = nullptr;     // [rows_cap] routing weight of each permuted row
   uint8_t* inter = nullptr;        // [rows_cap][4096] two-term e4m3 intermediate (hi | lo)
   float* inter_scale = nullptr;    // [16][rows_cap] hi scales (lo = hi / 16)
-  float* g_part = nullptr;         // [kMaxSplitMTiles*128][4096] split-K partial sums
-  int32_t* tile_sem = nullptr;     // [kMaxSplitMTiles][16] split-K arrival counters
-  float* accum = nullptr;          // [t_cap][7168] fp32 combine accumulator (kept zero between calls)
+  float* g_part = nullptr;         // [kMaxSplitMTiles*128][4096] GEMM1 split-K partial sums (kept zero)
+  int32_t* tile_sem = nullptr;     // [kMaxSplitMTiles][16] GEMM1 split-K arrival counters (kept zero)
+  float* g2_part = nullptr;        // [kMaxSplitMTiles*128][7168] GEMM2 split-K partial sums (kept zero)
+  int32_t* tile_sem2 = nullptr;    // [kMaxSplitMTiles][28] GEMM2 split-K arrival counters (kept zero)
+  float* out_rows = nullptr;       // [rows_cap][7168] routing-weighted expert output of every permuted row
+  int32_t* token_rows = nullptr;   // [t_cap][8] permuted rows of each token, ascending expert id, -1 padded
   unsigned* status = nullptr;      // device status word (kErrTimeout ...)
   void* base = nullptr;            // single allocation backing everything above
   size_t bytes = 0;
@@ -91,5 +94,6 @@ cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CU
 cudaError_t launch_gemm2(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
                          const float* w_scale, cudaStream_t s);
 cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32, cudaStream_t s);
+
 
 }  // namespace moe

@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
     };
     const int sp = lane + 1;
     const long long c1 = (total <= kMaxSplitMTiles) ? cost(total * kNT1, kKB1, 14, sp) : (sp == 1 ? 0 : 0x7fffffffffffLL);
-    const long long c2 = cost(total * kNT2, kKB2, 8, sp);
+    const long long c2 = (total <= kMaxSplitMTiles) ? cost(total * kNT2, kKB2, 8, sp) : (sp == 1 ? 0 : 0x7fffffffffffLL);
     // pack (cost, split) so that the minimum prefers the smaller split on ties
     unsigned long long k1 = (static_cast<unsigned long long>(c1) << 8) | sp;
     unsigned long long k2 = (static_cast<unsigned long long>(c2) << 8) | sp;
@@ -237,6 +237,23 @@ __global__ void __launch_bounds__(256) permute_kernel(PermuteArgs a, Workspace w
       w = ws.topk_w[o];
     }
   }
+  // token_rows[t]: this token's rows in ascending expert id (the order in which
+  // ref_moe.py:134-166 accumulates the experts), -1 padded
+  {
+    const int my_e = (row >= 0) ? ws.topk_ids[(size_t)t * kTopK + lane] : 0x7fffffff;
+    int rank = 0, n_loc = 0;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      const int ek = __shfl_sync(0xffffffffu, my_e, k);
+      const int rk = __shfl_sync(0xffffffffu, row, k);
+      rank += (rk >= 0 && (ek < my_e || (ek == my_e && k < lane))) ? 1 : 0;
+      n_loc += (rk >= 0) ? 1 : 0;
+    }
+    if (lane < kTopK) {
+      if (row >= 0) ws.token_rows[(size_t)t * kTopK + rank] = row;
+      if (lane >= n_loc) ws.token_rows[(size_t)t * kTopK + lane] = -1;
+    }
+  }
   const unsigned has = __ballot_sync(0xffffffffu, row >= 0);
   if (!has) return;
   const uint4* src = reinterpret_cast<const uint4*>(a.hidden + (size_t)t * kHidden);
@@ -263,24 +280,39 @@ __global__ void __launch_bounds__(256) permute_kernel(PermuteArgs a, Workspace w
   }
 }
 
-// out = cast(accum); accum = 0. Eight elements per thread.
-__global__ void __launch_bounds__(256) finalize_kernel(float* __restrict__ accum, void* __restrict__ out,
-                                                       int64_t n8, int out_fp32) {
+// out[t, :] = sum over the token's local rows (ascending expert id) of the
+// routing-weighted expert outputs, in fp32, then cast once (ref_moe.py:166-167).
+// Eight columns per thread.
+__global__ void __launch_bounds__(256) finalize_kernel(const float* __restrict__ rows_buf,
+                                                       const int32_t* __restrict__ token_rows,
+                                                       void* __restrict__ out, int T, int out_fp32) {
   griddep_wait();
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
-    float4* p = reinterpret_cast<float4*>(accum) + 2 * i;
-    float4 x0 = p[0], x1 = p[1];
-    p[0] = make_float4(0.f, 0.f, 0.f, 0.f);
-    p[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  constexpr int kC8 = kHidden / 8;  // 896 eight-column chunks per token
+  const int64_t n = (int64_t)T * kC8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = static_cast<int>(i / kC8);
+    const int c8 = static_cast<int>(i - (int64_t)t * kC8);
+    float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
+    const int4* tr = reinterpret_cast<const int4*>(token_rows + (size_t)t * kTopK);
+    const int4 r0 = __ldg(tr), r1 = __ldg(tr + 1);
+    const int r[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      if (r[k] < 0) break;
+      const float4* src = reinterpret_cast<const float4*>(rows_buf + (size_t)r[k] * kHidden) + 2 * c8;
+      const float4 a = __ldcs(src), b = __ldcs(src + 1);
+      s0.x += a.x; s0.y += a.y; s0.z += a.z; s0.w += a.w;
+      s1.x += b.x; s1.y += b.y; s1.z += b.z; s1.w += b.w;
+    }
     if (out_fp32) {
       float4* o = reinterpret_cast<float4*>(out) + 2 * i;
-      o[0] = x0;
-      o[1] = x1;
+      o[0] = s0;
+      o[1] = s1;
     } else {
-      __nv_bfloat162 b0 = __floats2bfloat162_rn(x0.x, x0.y);
-      __nv_bfloat162 b1 = __floats2bfloat162_rn(x0.z, x0.w);
-      __nv_bfloat162 b2 = __floats2bfloat162_rn(x1.x, x1.y);
-      __nv_bfloat162 b3 = __floats2bfloat162_rn(x1.z, x1.w);
+      __nv_bfloat162 b0 = __floats2bfloat162_rn(s0.x, s0.y);
+      __nv_bfloat162 b1 = __floats2bfloat162_rn(s0.z, s0.w);
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(s1.x, s1.y);
+      __nv_bfloat162 b3 = __floats2bfloat162_rn(s1.z, s1.w);
       uint4 u;
       u.x = *reinterpret_cast<uint32_t*>(&b0);
       u.y = *reinterpret_cast<uint32_t*>(&b1);
@@ -332,8 +364,10 @@ cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32,
   const int64_t n8 = (int64_t)T * kHidden / 8;
   if (n8 == 0) return cudaSuccess;
   int64_t blocks = (n8 + 255) / 256;
-  if (blocks > 8 * kSMs) blocks = 8 * kSMs;
-  return launch_k(finalize_kernel, dim3((unsigned)blocks), dim3(256), 0, s, true, ws.accum, out, n8, out_fp32);
+  if (blocks > 16 * kSMs) blocks = 16 * kSMs;
+  return launch_k(finalize_kernel, dim3((unsigned)blocks), dim3(256), 0, s, true,
+                  static_cast<const float*>(ws.out_rows), static_cast<const int32_t*>(ws.token_rows), out, T,
+                  out_fp32);
 }
 
 }  // namespace moe
