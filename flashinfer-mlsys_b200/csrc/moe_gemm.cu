@@ -424,15 +424,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (ctl->fixup_flag) {
             __threadfence();
             if (valid) {
+              // all loads first (independent), then clear the scratch
+              float4* pg = reinterpret_cast<float4*>(g + x.n * kBlk + cg * 32);
+              float4* pu = reinterpret_cast<float4*>(g + kInter + x.n * kBlk + cg * 32);
 #pragma unroll
-              for (int i = 0; i < 32; i += 4) {
-                float4* pg = reinterpret_cast<float4*>(g + x.n * kBlk + cg * 32 + i);
-                float4* pu = reinterpret_cast<float4*>(g + kInter + x.n * kBlk + cg * 32 + i);
-                const float4 a4 = __ldcg(pg), b4 = __ldcg(pu);
-                acc[i] = a4.x; acc[i + 1] = a4.y; acc[i + 2] = a4.z; acc[i + 3] = a4.w;
-                acc[32 + i] = b4.x; acc[33 + i] = b4.y; acc[34 + i] = b4.z; acc[35 + i] = b4.w;
-                __stcg(pg, make_float4(0.f, 0.f, 0.f, 0.f));
-                __stcg(pu, make_float4(0.f, 0.f, 0.f, 0.f));
+              for (int i = 0; i < 8; ++i) {
+                const float4 a4 = __ldcg(pg + i), b4 = __ldcg(pu + i);
+                acc[4 * i] = a4.x; acc[4 * i + 1] = a4.y; acc[4 * i + 2] = a4.z; acc[4 * i + 3] = a4.w;
+                acc[32 + 4 * i] = b4.x; acc[33 + 4 * i] = b4.y; acc[34 + 4 * i] = b4.z; acc[35 + 4 * i] = b4.w;
+              }
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                __stcg(pg + i, make_float4(0.f, 0.f, 0.f, 0.f));
+                __stcg(pu + i, make_float4(0.f, 0.f, 0.f, 0.f));
               }
             }
             swiglu_quant_store(acc, acc + 32, cg, row_in_tile, valid, row, x.n, ctl, p, es);
@@ -467,10 +471,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (ctl->fixup_flag) {
             __threadfence();
             if (valid) {
+              // all loads first (independent), then the stores
               float4* pg = reinterpret_cast<float4*>(g);
+              float4 v[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) v[i] = __ldcg(pg + i);
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
-                dst[i] = __ldcg(pg + i);
+                dst[i] = v[i];
                 __stcg(pg + i, make_float4(0.f, 0.f, 0.f, 0.f));
               }
             }
