@@ -97,6 +97,29 @@ int moe_fp8_ds_route(const float* routing_logits, const void* routing_bias,
                      int32_t* expert_counts_out, void* stream);
 
 /*
+ * Allocation-free routing. No counterpart in the reference: it exists for
+ * callers that cannot call cudaMalloc when they route (a process whose device
+ * memory is owned by a fixed-size pool or arena, an engine that reserves all
+ * memory at start-up, or code that must not take the CUDA allocator's locks on
+ * its hot path). Same arguments, outputs and status codes as
+ * moe_fp8_ds_route(), but all scratch lives in one fixed array of 1,052,416
+ * bytes in the library's own device memory, present on every GPU that loads
+ * the library until the process exits; the call makes no allocation of any
+ * kind. Limits: seq_len <= 8192 (larger requests return MOE_ERR_INVALID_ARG
+ * and launch nothing); num_local_experts in {32, 64, 128, 256}.
+ * The first call on a device looks up the array's device address (once per
+ * device); make that first call before capturing a stream into a CUDA graph.
+ * Every call reuses the same array: calls that may run at the same time on the
+ * GPU (different streams without ordering, or different host threads) race on
+ * it and must be serialised by the caller.
+ */
+int moe_fp8_ds_route_noalloc(const float* routing_logits, const void* routing_bias,
+                             int64_t seq_len, int64_t local_expert_offset,
+                             int64_t num_local_experts, double routed_scaling_factor,
+                             int32_t* topk_ids_out, float* topk_weights_out,
+                             int32_t* expert_counts_out, void* stream);
+
+/*
  * Expert computation for pre-routed tokens (the expert loop of
  * kernel.cu:235-291 / ref_moe.py:131-167, without the routing step). Used by
  * the expert-parallel layer on the rank that owns the experts:
