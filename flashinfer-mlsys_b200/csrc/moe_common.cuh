@@ -49,10 +49,10 @@ constexpr int kStageA = kTileM * kBlk;        // 16 KB of e4m3
 constexpr int kStageB = kTileN * kBlk;        // 32 KB of e4m3
 constexpr int kStageBytes = kStageA + kStageB;
 
-constexpr int kGemmThreads = 608;             // 19 warps
+constexpr int kGemmThreads = 384;             // 12 warps (168 registers per thread)
 constexpr int kScaleWarp = 2;                 // warp 2 streams block scales into shared memory
-constexpr int kEpiWarp0 = 3;                  // warps 3..18 run the epilogue
-constexpr int kEpiWarps = 16;
+constexpr int kEpiWarp0 = 4;                  // warps 4..11 run the epilogue (warp 3 idles)
+constexpr int kEpiWarps = 8;                  // two per TMEM lane quarter, 128 columns each
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kScaleSlots = 8;                // depth of the scale ring (K blocks ahead)
 
@@ -178,6 +178,24 @@ __device__ __forceinline__ void mma_f8f6f4(uint32_t d_tmem, uint64_t a_desc, uin
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i of the warp receives row
+// (lane base + i), columns [col, col+32). Waits for completion.
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // 32 lanes x 16 consecutive 32-bit columns: thread i of the warp receives row
