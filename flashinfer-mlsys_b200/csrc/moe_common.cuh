@@ -49,10 +49,10 @@ constexpr int kStageA = kTileM * kBlk;        // 16 KB of e4m3
 constexpr int kStageB = kTileN * kBlk;        // 32 KB of e4m3
 constexpr int kStageBytes = kStageA + kStageB;
 
-constexpr int kGemmThreads = 384;             // 12 warps (168 registers per thread)
+constexpr int kGemmThreads = 608;             // 19 warps
 constexpr int kScaleWarp = 2;                 // warp 2 streams block scales into shared memory
-constexpr int kEpiWarp0 = 4;                  // warps 4..11 run the epilogue (warp 3 idles)
-constexpr int kEpiWarps = 8;                  // two per TMEM lane quarter, 128 columns each
+constexpr int kEpiWarp0 = 3;                  // warps 3..18 run the epilogue
+constexpr int kEpiWarps = 16;                 // four per TMEM lane quarter, 64 columns each
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kScaleSlots = 8;                // depth of the scale ring (K blocks ahead)
 
@@ -109,12 +109,15 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+// One try_wait with a suspend-time hint: the thread sleeps in hardware until
+// the phase completes or the hint (ns) expires, instead of spinning on issue
+// slots the working warps need.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity, uint32_t hint_ns = 1000000u) {
   uint32_t ok;
   asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
 }
@@ -123,11 +126,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // not completed within ~limit_ns of wall time.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = global_timer_ns();
-  uint32_t n = 0;
+  const uint64_t t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++n & 255u) == 0u && global_timer_ns() - t0 > limit_ns) return false;
+    if (global_timer_ns() - t0 > limit_ns) return false;
   }
 }
 

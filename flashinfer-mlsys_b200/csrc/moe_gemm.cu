@@ -10,7 +10,7 @@
 //     blocks (16 hi + 16 lo, both against the same W2 block), then
 //     accum[token(r), :] += routing_weight(r) * O[r, :]  (ref_moe.py:162-166).
 //
-// Warp roles (384 threads, one CTA per SM):
+// Warp roles (576 threads, one CTA per SM):
 //   warp 0      TMA producer (one elected lane): A tile 128x128 + two B slabs
 //               128x128 per K block into a 4-stage shared-memory ring.
 //   warp 1      TMEM owner + MMA issuer (one lane): 4 x tcgen05.mma
@@ -19,13 +19,11 @@
 //   warp 2      scale loader: cp.async copies of the 128 row scales and the
 //               weight-block scales of every K block into an 8-deep shared
 //               ring, running ahead of the epilogue.
-//   warps 4-11  epilogue (two warps per TMEM lane quarter, 128 columns
-//               each): per K block, read the fresh partial from TMEM and
+//   warps 3-18  epilogue: per K block, read the fresh partial from TMEM and
 //               promote it in fp32 registers with a_scale[row,kb] *
 //               w_scale[nblk,kb] (the block scales are arbitrary fp32, so no
 //               hardware block-scale mode applies); after the last K block
-//               run the fused output stage. Only lane 0 of a warp polls a
-//               barrier; the others wait at __syncwarp.
+//               run the fused output stage.
 // Work units (expert, m-tile, n-tile, k-split) come from the device-side plan
 // written by the routing kernel; CTAs walk them with a static stride.
 #include "moe_kernels.h"
@@ -94,13 +92,13 @@ struct __align__(16) SmemCtl {
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t mma_done;
-  uint64_t epi_bar;   // barrier among the epilogue warps (bounded waits)
+  uint64_t epi_bar;   // barrier among the 16 epilogue warps (bounded waits)
   uint32_t tmem_base;
   int abort_flag;
   int fixup_flag;
   int prefix[kExperts + 1];
   int count[kExperts];
-  float amax[2][kTileM];
+  float amax[4][kTileM];
 };
 
 __device__ __forceinline__ void signal_abort(SmemCtl* c, unsigned* status) {
@@ -109,16 +107,6 @@ __device__ __forceinline__ void signal_abort(SmemCtl* c, unsigned* status) {
 }
 __device__ __forceinline__ bool aborted(SmemCtl* c) { return *reinterpret_cast<volatile int*>(&c->abort_flag) != 0; }
 
-// Whole-warp bounded wait: lane 0 polls the barrier, the other lanes wait at
-// __syncwarp (which also orders their later accesses after lane 0's acquire).
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
-  bool ok = true;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait_bounded(bar, parity, kWaitLimitNs);
-  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-  __syncwarp();
-  return ok;
-}
-
 // Barrier among the epilogue warps built on an mbarrier so that every wait is
 // bounded (a plain bar.sync could never give up). Returns false on timeout.
 struct EpiSync {
@@ -126,8 +114,9 @@ struct EpiSync {
   __device__ __forceinline__ bool sync(SmemCtl* c, unsigned* status) {
     __syncwarp();
     if ((threadIdx.x & 31) == 0) mbar_arrive(&c->epi_bar);
-    const bool ok = warp_wait(&c->epi_bar, phase);
+    bool ok = mbar_wait_bounded(&c->epi_bar, phase, kWaitLimitNs);
     phase ^= 1u;
+    ok = __all_sync(0xffffffffu, ok);
     if (!ok) signal_abort(c, status);
     return ok;
   }
@@ -141,49 +130,50 @@ __device__ __forceinline__ float e4m3_byte_to_f32(uint32_t b) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu)));
 }
 
-// SwiGLU of this thread's 64 (gate, up) pairs of one row (acc[0..63] gate,
-// acc[64..127] up) and two-term e4m3 quantisation of the 128-wide
-// intermediate block, whose other 64 columns belong to the partner warp.
-__device__ __forceinline__ void swiglu_quant_store(float* acc, int h, int row_in_tile, bool valid, size_t row,
-                                                   int n, SmemCtl* ctl, const GemmArgs& p, EpiSync& es) {
+// SwiGLU of 32 (gate, up) pairs of one row + two-term e4m3 quantisation of the
+// 128-wide intermediate block shared by the 4 column-group warps of the row.
+__device__ __forceinline__ void swiglu_quant_store(const float* gate, const float* up, int cg, int row_in_tile,
+                                                   bool valid, size_t row, int n, SmemCtl* ctl,
+                                                   const GemmArgs& p, EpiSync& es) {
+  float c[32];
   float amax = 0.f;
 #pragma unroll
-  for (int i = 0; i < 64; ++i) {
-    acc[i] = acc[i] * silu_ref(acc[64 + i]);
-    amax = fmaxf(amax, fabsf(acc[i]));
+  for (int i = 0; i < 32; ++i) {
+    c[i] = gate[i] * silu_ref(up[i]);
+    amax = fmaxf(amax, fabsf(c[i]));
   }
-  ctl->amax[h][row_in_tile] = amax;
+  ctl->amax[cg][row_in_tile] = amax;
   if (!es.sync(ctl, p.status)) return;
-  amax = fmaxf(ctl->amax[0][row_in_tile], ctl->amax[1][row_in_tile]);
+  amax = fmaxf(fmaxf(ctl->amax[0][row_in_tile], ctl->amax[1][row_in_tile]),
+               fmaxf(ctl->amax[2][row_in_tile], ctl->amax[3][row_in_tile]));
   if (!es.sync(ctl, p.status)) return;
   if (!valid) return;
   const float inv = amax > 0.f ? 448.0f / amax : 0.f;
   const float scale = amax / 448.0f;
-  uint8_t* base = p.inter + row * kInterCols + n * kBlk + h * 64;
+  uint32_t hi_w[8], lo_w[8];
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    uint32_t hw = 0, lw = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j += 2) {
+      const float u0 = c[i + j] * inv, u1 = c[i + j + 1] * inv;
+      const uint16_t h = f2_to_e4m3x2(u0, u1);
+      const float q0 = e4m3_byte_to_f32(h & 0xFFu), q1 = e4m3_byte_to_f32(h >> 8);
+      const uint16_t l = f2_to_e4m3x2((u0 - q0) * 16.0f, (u1 - q1) * 16.0f);
+      hw |= static_cast<uint32_t>(h) << (8 * j);
+      lw |= static_cast<uint32_t>(l) << (8 * j);
+    }
+    hi_w[i / 4] = hw;
+    lo_w[i / 4] = lw;
+  }
+  uint8_t* base = p.inter + row * kInterCols + n * kBlk + cg * 32;
   uint4* dh = reinterpret_cast<uint4*>(base);
   uint4* dl = reinterpret_cast<uint4*>(base + kInter);
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {  // 16 columns -> one 16-byte store of hi and of lo
-    uint32_t hw[4], lw[4];
-#pragma unroll
-    for (int i = 0; i < 16; i += 4) {
-      uint32_t a = 0, b = 0;
-#pragma unroll
-      for (int j = 0; j < 4; j += 2) {
-        const float u0 = acc[16 * c + i + j] * inv, u1 = acc[16 * c + i + j + 1] * inv;
-        const uint16_t hq = f2_to_e4m3x2(u0, u1);
-        const float q0 = e4m3_byte_to_f32(hq & 0xFFu), q1 = e4m3_byte_to_f32(hq >> 8);
-        const uint16_t lq = f2_to_e4m3x2((u0 - q0) * 16.0f, (u1 - q1) * 16.0f);
-        a |= static_cast<uint32_t>(hq) << (8 * j);
-        b |= static_cast<uint32_t>(lq) << (8 * j);
-      }
-      hw[i / 4] = a;
-      lw[i / 4] = b;
-    }
-    dh[c] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    dl[c] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-  }
-  if (h == 0) p.inter_scale[(size_t)n * p.rows_cap + row] = scale;
+  dh[0] = make_uint4(hi_w[0], hi_w[1], hi_w[2], hi_w[3]);
+  dh[1] = make_uint4(hi_w[4], hi_w[5], hi_w[6], hi_w[7]);
+  dl[0] = make_uint4(lo_w[0], lo_w[1], lo_w[2], lo_w[3]);
+  dl[1] = make_uint4(lo_w[4], lo_w[5], lo_w[6], lo_w[7]);
+  if (cg == 0) p.inter_scale[(size_t)n * p.rows_cap + row] = scale;
 }
 
 template <int kMode>
@@ -344,27 +334,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     cp_async_wait_all();
   } else {
-    // ======================= epilogue (8 warps) =======================
-    if (warp >= kEpiWarp0) {
-    const int q = warp & 3;                  // TMEM lane quarter accessible to this warp
-    const int h = (warp - kEpiWarp0) >> 2;   // column half 0..1
+    // ======================= epilogue (16 warps) =======================
+    const int q = warp & 3;              // TMEM lane quarter accessible to this warp
+    const int cg = (warp - kEpiWarp0) >> 2;  // column group 0..3
     const int row_in_tile = q * 32 + lane;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(q * 32) << 16);
     uint32_t gkb = 0;
     EpiSync es;
-    float acc[128];
+    float acc[64];
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
       if (aborted(ctl)) break;
       const Unit x = decode_unit<kMode>(u, split, ctl->prefix, ctl->count, E_l);
       const size_t row = (size_t)x.gm * kTileM + row_in_tile;
       const bool valid = row_in_tile < x.rows;
 #pragma unroll
-      for (int i = 0; i < 128; ++i) acc[i] = 0.f;
+      for (int i = 0; i < 64; ++i) acc[i] = 0.f;
       bool ok = true;
       for (int kb = x.kb0; kb < x.kb1; ++kb, ++gkb) {
         const uint32_t buf = gkb & 1u;
         const int j = gkb % kScaleSlots;
-        if (!warp_wait(&ctl->sfull[j], (gkb / kScaleSlots) & 1u)) {
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&ctl->sfull[j], (gkb / kScaleSlots) & 1u, kWaitLimitNs))) {
           signal_abort(ctl, p.status);
           ok = false;
           break;
@@ -377,29 +366,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             f0 = as * sl->w[0];
             f1 = as * sl->w[1];
           } else {
-            f0 = f1 = as * ((kb >= kInterBlocks) ? kLoScale : 1.0f) * sl->w[h];
+            f0 = f1 = as * ((kb >= kInterBlocks) ? kLoScale : 1.0f) * sl->w[cg >> 1];
           }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl->sempty[j]);
-        if (!warp_wait(&ctl->tfull[buf], (gkb >> 1) & 1u)) {
+        const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(&ctl->tfull[buf], (gkb >> 1) & 1u, kWaitLimitNs));
+        if (!got) {
           signal_abort(ctl, p.status);
           ok = false;
           break;
         }
+        __syncwarp();
         tc_fence_after();
         const uint32_t tb = t_lane + buf * kTileN;
-        // columns of this warp: GEMM1 gate [64h, 64h+64) -> acc[0..63] and up
-        // [128+64h, ...) -> acc[64..127]; GEMM2 [128h, 128h+128)
+        // columns of this warp: GEMM1 gate [32cg, 32cg+32) and up [128+32cg, ...);
+        // GEMM2 [64cg, 64cg+64)
+        const uint32_t c0 = (kMode == 1) ? cg * 32 : cg * 64;
+        const uint32_t c1 = (kMode == 1) ? kBlk + cg * 32 : cg * 64 + 32;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          const uint32_t col = (kMode == 1) ? ((c < 2) ? 64 * h + 32 * c : kBlk + 64 * h + 32 * (c - 2))
-                                            : 128 * h + 32 * c;
-          const float f = (c < 2) ? f0 : f1;
-          tmem_ld_32x32b_x32(tb + col, v);
+        for (int h = 0; h < 4; ++h) {
+          float v[16];
+          const uint32_t col = (h < 2) ? c0 + 16 * h : c1 + 16 * (h - 2);
+          const float f = (h < 2) ? f0 : f1;
+          tmem_ld_32x32b_x16(tb + col, v);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) acc[32 * c + i] = fmaf(f, v[i], acc[32 * c + i]);
+          for (int i = 0; i < 16; ++i) acc[16 * h + i] = fmaf(f, v[i], acc[16 * h + i]);
         }
         tc_fence_before();
         __syncwarp();
@@ -409,17 +401,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
       if (kMode == 1) {
         if (split == 1) {
-          swiglu_quant_store(acc, h, row_in_tile, valid, row, x.n, ctl, p, es);
+          swiglu_quant_store(acc, acc + 32, cg, row_in_tile, valid, row, x.n, ctl, p, es);
         } else {
           // split-K: reduce promoted partials in fp32 scratch; the last
           // arriving CTA of this (m-tile, n-tile) runs SwiGLU + quantisation.
-          float* gg = p.g_part + row * kGemm1N + x.n * kBlk + 64 * h;
-          float* gu = gg + kInter;
+          float* g = p.g_part + row * kGemm1N;
           if (valid) {
 #pragma unroll
-            for (int i = 0; i < 64; i += 4) {
-              red_add_v4(gg + i, acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
-              red_add_v4(gu + i, acc[64 + i], acc[65 + i], acc[66 + i], acc[67 + i]);
+            for (int i = 0; i < 32; i += 4) {
+              red_add_v4(g + x.n * kBlk + cg * 32 + i, acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+              red_add_v4(g + kInter + x.n * kBlk + cg * 32 + i, acc[32 + i], acc[33 + i], acc[34 + i],
+                         acc[35 + i]);
             }
           }
           __threadfence();
@@ -433,40 +425,40 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             __threadfence();
             if (valid) {
               // all loads first (independent), then clear the scratch
-              float4* pg = reinterpret_cast<float4*>(gg);
-              float4* pu = reinterpret_cast<float4*>(gu);
+              float4* pg = reinterpret_cast<float4*>(g + x.n * kBlk + cg * 32);
+              float4* pu = reinterpret_cast<float4*>(g + kInter + x.n * kBlk + cg * 32);
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
+              for (int i = 0; i < 8; ++i) {
                 const float4 a4 = __ldcg(pg + i), b4 = __ldcg(pu + i);
                 acc[4 * i] = a4.x; acc[4 * i + 1] = a4.y; acc[4 * i + 2] = a4.z; acc[4 * i + 3] = a4.w;
-                acc[64 + 4 * i] = b4.x; acc[65 + 4 * i] = b4.y; acc[66 + 4 * i] = b4.z; acc[67 + 4 * i] = b4.w;
+                acc[32 + 4 * i] = b4.x; acc[33 + 4 * i] = b4.y; acc[34 + 4 * i] = b4.z; acc[35 + 4 * i] = b4.w;
               }
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
+              for (int i = 0; i < 8; ++i) {
                 __stcg(pg + i, make_float4(0.f, 0.f, 0.f, 0.f));
                 __stcg(pu + i, make_float4(0.f, 0.f, 0.f, 0.f));
               }
             }
-            swiglu_quant_store(acc, h, row_in_tile, valid, row, x.n, ctl, p, es);
+            swiglu_quant_store(acc, acc + 32, cg, row_in_tile, valid, row, x.n, ctl, p, es);
             if (warp == kEpiWarp0 && lane == 0) p.tile_sem[x.gm * kNT1 + x.n] = 0;
           }
         }
       } else {
         const float w = valid ? __ldg(p.row_weight + row) : 0.f;
-        float4* dst = reinterpret_cast<float4*>(p.out_rows + row * kHidden + x.n * kTileN + 128 * h);
+        float4* dst = reinterpret_cast<float4*>(p.out_rows + row * kHidden + x.n * kTileN + cg * 64);
         if (split == 1) {
           if (valid) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
+            for (int i = 0; i < 16; ++i)
               dst[i] = make_float4(w * acc[4 * i], w * acc[4 * i + 1], w * acc[4 * i + 2], w * acc[4 * i + 3]);
           }
         } else {
           // split-K: partial sums meet in fp32 scratch; the last arriving CTA
           // of this (m-tile, n-tile) writes the finished rows.
-          float* g = p.g2_part + row * kHidden + x.n * kTileN + 128 * h;
+          float* g = p.g2_part + row * kHidden + x.n * kTileN + cg * 64;
           if (valid) {
 #pragma unroll
-            for (int i = 0; i < 128; i += 4)
+            for (int i = 0; i < 64; i += 4)
               red_add_v4(g + i, w * acc[i], w * acc[i + 1], w * acc[i + 2], w * acc[i + 3]);
           }
           __threadfence();
@@ -479,15 +471,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (ctl->fixup_flag) {
             __threadfence();
             if (valid) {
+              // all loads first (independent), then the stores
               float4* pg = reinterpret_cast<float4*>(g);
+              float4 v[16];
 #pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const float4 v4 = __ldcg(pg + i);
-                acc[4 * i] = v4.x; acc[4 * i + 1] = v4.y; acc[4 * i + 2] = v4.z; acc[4 * i + 3] = v4.w;
-              }
+              for (int i = 0; i < 16; ++i) v[i] = __ldcg(pg + i);
 #pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                dst[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+              for (int i = 0; i < 16; ++i) {
+                dst[i] = v[i];
                 __stcg(pg + i, make_float4(0.f, 0.f, 0.f, 0.f));
               }
             }
@@ -495,7 +486,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
-    }
     }
   }
 
