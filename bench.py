@@ -31,6 +31,8 @@ WORKLOADS = {
     "decode_sweep": ((1, 2, 4, 8, 16, 32, 64), "BASELINE configs[1]: decode sweep, 32 local experts, offset 0"),
     "mid": ((256, 1024), "BASELINE configs[2]: mid prefill, near-uniform routing"),
     "large": ((4096, 8192, 16384), "BASELINE configs[3]: large prefill, +2.0 bias on 4 hot local experts"),
+    "ep": ((4096,), "BASELINE configs[4]: full 256-expert layer, expert parallel, 4096 tokens per GPU, "
+                    "NCCL all-to-all dispatch/combine"),
 }
 L2_FLUSH_BYTES = 256 << 20
 
@@ -328,6 +330,10 @@ def cpu_baseline(Ts, acts, w):
 
 
 def bench_reference(args):
+    """The reference algorithm on the host CPU (oracle port, BLAS on all cores).
+    One step = one oracle call on a bounded token sample of one workload point:
+    the whole batch when T <= 64, else 64 of its tokens with the time scaled by
+    T / 64 (each output row depends only on its own token)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -336,39 +342,165 @@ def bench_reference(args):
     Ts, wdesc = WORKLOADS[args.workload]
     if args.T:
         Ts = tuple(int(t) for t in args.T.split(","))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    e_local = 256 if args.workload == "ep" else 32
     cache = {}
 
     def get_expert(le):
         if le not in cache:
-            q13, s13, q2, s2 = wl.expert_weights(le, "cpu", 0)
-            cache[le] = (q13, s13, q2, s2)
+            cache[le] = wl.expert_weights(le, "cpu", 0)
         return cache[le]
 
-    acts = {T: wl.config_activations(T) for T in Ts}
+    SAMPLE = 64
+    acts, subset = {}, {}
+    for T in Ts:
+        acts[T] = (wl.make_activations(T, seed=T) if args.workload == "ep" else wl.config_activations(T))
+        subset[T] = None if T <= SAMPLE else list(range(0, T, T // SAMPLE))[:SAMPLE]
     seq = [Ts[i % len(Ts)] for i in range(args.warmup + args.steps)]
-    # weights generation is setup, not the reference's work
+    # weight generation is setup, not the reference's work
     for T in set(seq):
         r = O.route(acts[T].logits.numpy(), O.as_f32(acts[T].bias), 2.5)
-        for le in set(int(x) for x in r["topk_idx"].ravel() if 0 <= x < 32):
+        rows = r["topk_idx"] if subset[T] is None else r["topk_idx"][subset[T]]
+        for le in set(int(x) for x in rows.ravel() if 0 <= x < e_local):
             get_expert(le)
     times = []
     for i, T in enumerate(seq):
         t0 = time.perf_counter()
-        _oracle_call(O, acts[T], get_expert)
+        O.moe_forward(acts[T].logits.numpy(), O.as_f32(acts[T].bias), O.as_u8(acts[T].hidden),
+                      acts[T].hidden_scale.numpy(), get_expert, 0, 2.5, e_local, token_subset=subset[T])
+        dt = time.perf_counter() - t0
+        if subset[T] is not None:
+            dt *= T / len(subset[T])
         if i >= args.warmup:
-            times.append((T, time.perf_counter() - t0))
-    us = statistics.mean(t for _, t in times) * 1e6
+            times.append(dt)
+    us = statistics.mean(times) * 1e6
+    sample = ("one oracle call per step, T cycling through " + str(list(Ts)) +
+              ("; T > 64 runs 64 of its tokens, time scaled by T/64" if max(Ts) > SAMPLE else ""))
     line = {
-        "metric": METRIC, "value": round(us, 1), "unit": "us/call", "impl": "reference", "n_gpus": 0,
+        "metric": METRIC, "value": round(us, 1), "unit": "us/call", "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 3), "higher_is_better": False,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32 (dequantised)", "data": "synthetic, seeded",
-        "config": {"workload": f"{args.workload}: {wdesc}", "T": list(Ts), "num_local_experts": 32,
+        "config": {"workload": f"{args.workload}: {wdesc}", "T": list(Ts), "num_local_experts": e_local,
                    "local_expert_offset": 0, "routed_scaling_factor": 2.5},
         "cpu_baseline": {"value": round(us, 1), "unit": "us/call", "cores": os.cpu_count(), "kind": "port",
-                         "sample": "one call per step, T cycling through the sweep"},
+                         "sample": sample},
         "e2e": {"value": round(us, 1), "unit": "us/call", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def bench_ep(args):
+    """every GPU holds 256/N experts and 4096 tokens of its
+    own; one step = one expert-parallel layer call on every rank (routing,
+    all-to-all dispatch, expert compute, all-to-all combine, fp32 sum)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    rank, world = _dist()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pkg = importlib.import_module("flashinfer-mlsys_b200")
+    wl = importlib.import_module("flashinfer-mlsys_b200.workloads")
+    ep = importlib.import_module("flashinfer-mlsys_b200.ep")
+    T = int(args.T) if args.T else 4096
+    e_local = 256 // world
+    offset = rank * e_local
+    w = wl.make_weights(e_local, offset, dev)
+    acts = wl.make_activations(T, seed=rank * 1_000_000 + T)
+    a = acts.to(dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    if world > 1:
+        experts_fn = ep.make_cuda_experts_fn(w.w13, w.s13, w.w2, w.s2)
+
+        def call(x):
+            return ep.ep_forward(x.logits, x.bias, x.hidden, x.hidden_scale, 2.5, ep.cuda_route_fn, experts_fn)
+    else:
+        out1 = torch.empty((T, 7168), dtype=torch.bfloat16, device=dev)
+
+        def call(x):
+            pkg.kernel(x.logits, x.bias, x.hidden, x.hidden_scale, w.w13, w.s13, w.w2, w.s2, 0, 2.5, out1)
+            return out1
+
+    # routing statistics of this rank's share (local pairs over all ranks' tokens)
+    ids, _, cnt = pkg.route(a.logits, a.bias, 0, 256, 2.5)
+    own = torch.zeros(1, dtype=torch.int64, device=dev)
+    pairs = torch.tensor([ids.numel()], dtype=torch.int64, device=dev)
+    if world > 1:
+        dist.all_reduce(pairs)
+    n_assign_total = int(pairs.item())  # 8 pairs per token over the whole job
+    for _ in range(args.warmup):
+        flush.zero_()
+        call(a)
+    torch.cuda.synchronize()
+    evs = []
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            call(a)
+            e1.record(stream)
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = statistics.mean(x.elapsed_time(y) for x, y in evs)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # end to end: H2D of this rank's inputs, the call, D2H of the output
+    host = [acts.logits.pin_memory(), acts.bias.pin_memory(), acts.hidden.view(torch.uint8).pin_memory(),
+            acts.hidden_scale.pin_memory()]
+    host_out = torch.empty((T, 7168), dtype=torch.bfloat16).pin_memory()
+    e2e = []
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        a.logits.copy_(host[0], non_blocking=True)
+        a.bias.copy_(host[1], non_blocking=True)
+        a.hidden.view(torch.uint8).copy_(host[2], non_blocking=True)
+        a.hidden_scale.copy_(host[3], non_blocking=True)
+        o = call(a)
+        host_out.copy_(o, non_blocking=True)
+        e1.record(stream)
+        if i >= args.warmup:
+            e2e.append((e0, e1))
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([statistics.mean(x.elapsed_time(y) for x, y in e2e)], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    flops = wl.moe_flops(n_assign_total)
+    hbm_peak, bf16_peak, peak_src = _peaks()
+    line = {
+        "metric": METRIC, "value": round(ms * 1e3, 2), "unit": "us/call", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 (tcgen05 kind::f8f6f4)",
+        "data": "synthetic, seeded (BASELINE value distributions)",
+        "config": {"workload": f"ep: {WORKLOADS['ep'][1]}", "T_per_gpu": T, "num_local_experts": e_local,
+                   "local_expert_offset": "rank*256/N", "routed_scaling_factor": 2.5,
+                   "combine": "bf16 partials, fp32 sum", "l2": "256 MB L2 flush before every call, outside events",
+                   "parallelism": f"ep{world}"},
+        "tflops": round(flops / (ms * 1e-3) / 1e12, 3),
+        "e2e": {"value": round(float(e2e_ms.item()) * 1e3, 2), "unit": "us/call",
+                "h2d_bytes_per_step": int(sum(x.numel() * x.element_size() for x in host)),
+                "d2h_bytes_per_step": T * 7168 * 2},
+        "gpu_launches": 6 * args.steps if world > 1 else 5 * args.steps,
+        "clocks": clk.summary(),
+        "peak_source": peak_src,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def main():
@@ -377,13 +509,19 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode_sweep")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=None,
+                    help="default: decode_sweep on 1 GPU, ep on N>1 GPUs")
     ap.add_argument("--T", default="", help="comma-separated token counts overriding the workload's sweep")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.workload is None:
+        args.workload = "ep" if world > 1 else "decode_sweep"
     if args.impl == "reference":
         bench_reference(args)
+    elif args.workload == "ep":
+        bench_ep(args)
     else:
         bench_ours(args)
 
