@@ -13,7 +13,10 @@ using namespace moe;
 namespace {
 
 std::mutex g_mu;
-std::unordered_map<int, Workspace> g_ws;  // per device
+// Cached workspaces, one per (device, layout): the full expert pipeline per
+// number of local experts, plus a small routing-only layout (key suffix 0).
+std::unordered_map<int64_t, Workspace> g_ws;
+inline int64_t ws_key(int dev, int e_local, bool routing_only) { return (int64_t)dev * 1024 + (routing_only ? 0 : e_local); }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -82,8 +85,8 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // Computes the layout; when `base` is non-null also assigns the pointers.
 // `zero_bytes` receives the length of the prefix that must start zeroed
 // (self-resetting counters, the combine accumulator, split-K scratch).
-size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_bytes) {
-  const int64_t rows = rows_cap_for(T, e_local);
+size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_bytes, bool routing_only = false) {
+  const int64_t rows = routing_only ? 0 : rows_cap_for(T, e_local);
   const int ctas = route_ctas_for(static_cast<int>(T));
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -95,6 +98,19 @@ size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_
   w.expert_fill = reinterpret_cast<int32_t*>(take((size_t)kExperts * 4));
   w.done_ctas = reinterpret_cast<uint32_t*>(take(4));
   w.status = reinterpret_cast<unsigned*>(take(4));
+  if (routing_only) {
+    if (zero_bytes) *zero_bytes = off;
+    w.plan = reinterpret_cast<Plan*>(take(sizeof(Plan)));
+    w.topk_ids = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
+    w.topk_w = reinterpret_cast<float*>(take(Tz * kTopK * 4));
+    w.topk_rank = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
+    w.cta_off = reinterpret_cast<int32_t*>(take((size_t)(ctas > 256 ? ctas : 256) * kExperts * 4));
+    w.rows_cap = 0;
+    w.t_cap = T;
+    w.e_local = e_local;
+    w.route_ctas_cap = ctas;
+    return off;
+  }
   w.tile_sem = reinterpret_cast<int32_t*>(take((size_t)kMaxSplitMTiles * kNT1 * 4));
   w.tile_sem2 = reinterpret_cast<int32_t*>(take((size_t)kMaxSplitMTiles * kNT2 * 4));
   w.g_part = reinterpret_cast<float*>(take((size_t)kMaxSplitMTiles * kTileM * kGemm1N * 4));
@@ -128,16 +144,15 @@ void forget_maps(const void* base, size_t bytes) {
   }
 }
 
-int get_workspace(int64_t T, int e_local, Workspace** out) {
+int get_workspace(int64_t T, int e_local, bool routing_only, Workspace** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MOE_ERR_CUDA;
-  Workspace& w = g_ws[dev];
-  if (w.base && w.t_cap >= T && w.e_local == e_local) {
+  Workspace& w = g_ws[ws_key(dev, e_local, routing_only)];
+  if (w.base && w.t_cap >= T) {
     *out = &w;
     return MOE_OK;
   }
   int64_t t_new = T;
-  if (w.base && w.e_local == e_local && w.t_cap > t_new) t_new = w.t_cap;
   if (w.base) {
     cudaDeviceSynchronize();
     forget_maps(w.base, w.bytes);
@@ -146,7 +161,7 @@ int get_workspace(int64_t T, int e_local, Workspace** out) {
   }
   Workspace nw;
   size_t zero_bytes = 0;
-  const size_t bytes = layout(nw, t_new, e_local, nullptr, &zero_bytes);
+  const size_t bytes = layout(nw, t_new, e_local, nullptr, &zero_bytes, routing_only);
   void* base = nullptr;
   if (cudaMalloc(&base, bytes) != cudaSuccess) {
     cudaGetLastError();
@@ -156,7 +171,7 @@ int get_workspace(int64_t T, int e_local, Workspace** out) {
     cudaFree(base);
     return MOE_ERR_CUDA;
   }
-  layout(nw, t_new, e_local, static_cast<uint8_t*>(base), nullptr);
+  layout(nw, t_new, e_local, static_cast<uint8_t*>(base), nullptr, routing_only);
   nw.base = base;
   nw.bytes = bytes;
   w = nw;
@@ -216,7 +231,7 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
 
   std::lock_guard<std::mutex> lk(g_mu);
   Workspace* ws = nullptr;
-  rc = get_workspace(T, static_cast<int>(E_l), &ws);
+  rc = get_workspace(T, static_cast<int>(E_l), route_only, &ws);
   if (rc) return rc;
 
   RouteArgs ra{};
@@ -329,15 +344,17 @@ int moe_fp8_ds_device_status(void* stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MOE_ERR_CUDA;
   std::lock_guard<std::mutex> lk(g_mu);
-  auto it = g_ws.find(dev);
-  if (it == g_ws.end() || !it->second.base) return MOE_OK;
-  unsigned v = 0;
-  if (cudaMemcpy(&v, it->second.status, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return MOE_ERR_CUDA;
-  if (v) {
-    cudaMemset(it->second.status, 0, 4);
-    return MOE_ERR_DEVICE_TIMEOUT;
+  int rc = MOE_OK;
+  for (auto& kv : g_ws) {
+    if (kv.first / 1024 != dev || !kv.second.base) continue;
+    unsigned v = 0;
+    if (cudaMemcpy(&v, kv.second.status, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return MOE_ERR_CUDA;
+    if (v) {
+      cudaMemset(kv.second.status, 0, 4);
+      rc = MOE_ERR_DEVICE_TIMEOUT;
+    }
   }
-  return MOE_OK;
+  return rc;
 }
 
 size_t moe_fp8_ds_workspace_bytes(int64_t seq_len, int64_t num_local_experts) {
@@ -350,12 +367,17 @@ int moe_fp8_ds_release_workspace(void) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MOE_ERR_CUDA;
   std::lock_guard<std::mutex> lk(g_mu);
-  auto it = g_ws.find(dev);
-  if (it != g_ws.end() && it->second.base) {
-    cudaDeviceSynchronize();
-    forget_maps(it->second.base, it->second.bytes);
-    cudaFree(it->second.base);
-    g_ws.erase(it);
+  cudaDeviceSynchronize();
+  for (auto it = g_ws.begin(); it != g_ws.end();) {
+    if (it->first / 1024 == dev) {
+      if (it->second.base) {
+        forget_maps(it->second.base, it->second.bytes);
+        cudaFree(it->second.base);
+      }
+      it = g_ws.erase(it);
+    } else {
+      ++it;
+    }
   }
   return MOE_OK;
 }

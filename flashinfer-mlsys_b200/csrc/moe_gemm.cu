@@ -135,11 +135,15 @@ __device__ __forceinline__ float e4m3_byte_to_f32(uint32_t b) {
 __device__ __forceinline__ void swiglu_quant_store(const float* gate, const float* up, int cg, int row_in_tile,
                                                    bool valid, size_t row, int n, SmemCtl* ctl,
                                                    const GemmArgs& p, EpiSync& es) {
+  // padding rows (past the expert's token count) hold garbage partials; keep
+  // them out of expf/division, whose special-value paths would stall the warp
   float c[32];
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
-    c[i] = gate[i] * silu_ref(up[i]);
+    const float g = valid ? gate[i] : 0.f;
+    const float u = valid ? up[i] : 0.f;
+    c[i] = g * silu_ref(u);
     amax = fmaxf(amax, fabsf(c[i]));
   }
   ctl->amax[cg][row_in_tile] = amax;
@@ -211,6 +215,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tensormap(&map_a);
     prefetch_tensormap(&map_w);
   }
+  // Weight tiles do not depend on the previous kernel: the producer issues
+  // the B (weight) loads of its first stages before waiting for it. The plan
+  // is already complete here (it was written by the routing kernel, which
+  // finished before the previous kernel released this one).
+  int n_pre = 0;
+  if (tid == 0) {
+    const int units0 = p.plan->total_mtiles * NT * ((kMode == 1) ? p.plan->split1 : p.plan->split2);
+    const int split0 = (kMode == 1) ? p.plan->split1 : p.plan->split2;
+    for (int u = blockIdx.x; u < units0 && n_pre < kStages; u += gridDim.x) {
+      const Unit x = decode_unit<kMode>(u, split0, p.plan->mtile_prefix, p.plan->count, E_l);
+      for (int kb = x.kb0; kb < x.kb1 && n_pre < kStages; ++kb, ++n_pre) {
+        uint8_t* sb = tiles + n_pre * kStageBytes + kStageA;
+        mbar_arrive_expect_tx(&ctl->full[n_pre], kStageBytes);
+        if (kMode == 1) {
+          const int y0 = x.e * kGemm1N + x.n * kBlk;
+          tma_load_2d(sb, &map_w, kb * kBlk, y0, &ctl->full[n_pre]);
+          tma_load_2d(sb + kStageA, &map_w, kb * kBlk, y0 + kInter, &ctl->full[n_pre]);
+        } else {
+          const int y0 = x.e * kHidden + x.n * kTileN;
+          const int kx = (kb % kInterBlocks) * kBlk;
+          tma_load_2d(sb, &map_w, kx, y0, &ctl->full[n_pre]);
+          tma_load_2d(sb + kStageA, &map_w, kx, y0 + kBlk, &ctl->full[n_pre]);
+        }
+      }
+    }
+  }
   if (warp == 1) {
     tmem_alloc(&ctl->tmem_base, 512);
     tmem_relinquish();
@@ -239,9 +269,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int kb = x.kb0; kb < x.kb1; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1u;
-          if (!mbar_wait_bounded(&ctl->empty[s], ph ^ 1u, kWaitLimitNs)) { signal_abort(ctl, p.status); break; }
           uint8_t* sa = tiles + s * kStageBytes;
           uint8_t* sb = sa + kStageA;
+          if (static_cast<int>(it) < n_pre) {
+            // weights of this stage are already in flight: add the token tile
+            tma_load_2d(sa, &map_a, kb * kBlk, x.gm * kTileM, &ctl->full[s]);
+            continue;
+          }
+          if (!mbar_wait_bounded(&ctl->empty[s], ph ^ 1u, kWaitLimitNs)) { signal_abort(ctl, p.status); break; }
           mbar_arrive_expect_tx(&ctl->full[s], kStageBytes);
           tma_load_2d(sa, &map_a, kb * kBlk, x.gm * kTileM, &ctl->full[s]);
           if (kMode == 1) {

@@ -15,7 +15,9 @@ namespace moe {
 
 namespace {
 
-constexpr int kRouteThreads = 256;  // 8 warps, one token per warp at a time
+constexpr int kRouteThreads = 256;      // 8 warps per CTA for multi-CTA routing
+constexpr int kRouteThreadsOne = 1024;  // a call with T <= 64 routes in one CTA of 32 warps
+constexpr int kOneCtaTokens = 64;
 
 // Sort 8 composite keys descending (19-comparator network, all-0/1-input verified).
 __device__ __forceinline__ void cmpswap(uint64_t& a, uint64_t& b) {
@@ -32,7 +34,7 @@ __device__ __forceinline__ void sort8_desc(uint64_t (&c)[8]) {
   cmpswap(c[1], c[2]); cmpswap(c[3], c[4]); cmpswap(c[5], c[6]);
 }
 
-__global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, Workspace ws) {
+__global__ void __launch_bounds__(kRouteThreadsOne) route_plan_kernel(RouteArgs a, Workspace ws) {
   __shared__ int hist[kExperts];
   __shared__ int is_last;
   const int tid = threadIdx.x;
@@ -46,7 +48,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
 
   const int t_begin = blockIdx.x * a.tokens_per_cta;
   const int t_end = min(a.T, t_begin + a.tokens_per_cta);
-  for (int t = t_begin + warp; t < t_end; t += kRouteThreads / 32) {
+  const int nwarps = blockDim.x >> 5;
+  for (int t = t_begin + warp; t < t_end; t += nwarps) {
     int my_id = -1;     // lane k < 8 holds the k-th selected expert
     float my_w = 0.f;
     if (a.logits != nullptr) {
@@ -146,23 +149,31 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
   }
   __syncthreads();
 
-  // ---- publish this CTA's histogram: its base slot inside every expert ----
-  for (int e = tid; e < E_l; e += blockDim.x) {
-    const int h = hist[e];
-    ws.cta_off[(size_t)blockIdx.x * E_l + e] = h ? atomicAdd(&ws.expert_fill[e], h) : 0;
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) is_last = (atomicAdd(ws.done_ctas, 1u) == gridDim.x - 1) ? 1 : 0;
-  __syncthreads();
-  if (!is_last) return;
-
-  // ---- last CTA: per-expert counts, m-tile prefix, K-split plan ----
-  __threadfence();
-  __shared__ int warp_tot[2][kRouteThreads / 32];
   int c = 0;
+  if (gridDim.x == 1) {
+    // single CTA: the shared histogram is the whole story
+    if (tid < E_l) {
+      c = hist[tid];
+      ws.cta_off[tid] = 0;
+    }
+  } else {
+    // ---- publish this CTA's histogram: its base slot inside every expert ----
+    for (int e = tid; e < E_l; e += blockDim.x) {
+      const int h = hist[e];
+      ws.cta_off[(size_t)blockIdx.x * E_l + e] = h ? atomicAdd(&ws.expert_fill[e], h) : 0;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) is_last = (atomicAdd(ws.done_ctas, 1u) == gridDim.x - 1) ? 1 : 0;
+    __syncthreads();
+    if (!is_last) return;
+    // ---- last CTA: per-expert counts ----
+    __threadfence();
+    if (tid < E_l) c = atomicExch(&ws.expert_fill[tid], 0);  // read and reset for the next call
+  }
+  // ---- m-tile prefix and K-split plan ----
+  __shared__ int warp_tot[2][kRouteThreadsOne / 32];
   if (tid < E_l) {
-    c = atomicExch(&ws.expert_fill[tid], 0);  // read and reset for the next call
     ws.plan->count[tid] = c;
     if (a.user_counts) a.user_counts[tid] = c;
   }
@@ -179,7 +190,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
   if (lane == 0) warp_tot[1][warp] = csum;
   __syncthreads();
   int base = 0, total = 0, nas = 0;
-  for (int w = 0; w < kRouteThreads / 32; ++w) {
+  for (int w = 0; w < nwarps; ++w) {
     if (w < warp) base += warp_tot[0][w];
     total += warp_tot[0][w];
     nas += warp_tot[1][w];
@@ -338,7 +349,8 @@ int device_sm_count() {
 }
 
 int tokens_per_cta_for(int T) {
-  // one token per warp for small T; at most ~kSMs routing CTAs for large T
+  // T <= 64: one CTA of 32 warps; otherwise at most ~kSMs CTAs of 8 warps
+  if (T <= kOneCtaTokens) return kOneCtaTokens;
   int per = (T + kSMs - 1) / kSMs;
   per = ((per + 7) / 8) * 8;
   return per < 8 ? 8 : per;
@@ -352,7 +364,8 @@ int route_ctas_for(int T) {
 
 cudaError_t launch_route(const Workspace& ws, const RouteArgs& a, cudaStream_t s) {
   const int grid = route_ctas_for(a.T);
-  return launch_k(route_plan_kernel, dim3(grid), dim3(kRouteThreads), 0, s, false, a, ws);
+  const int threads = (grid == 1) ? kRouteThreadsOne : kRouteThreads;
+  return launch_k(route_plan_kernel, dim3(grid), dim3(threads), 0, s, false, a, ws);
 }
 
 cudaError_t launch_permute(const Workspace& ws, const PermuteArgs& a, cudaStream_t s) {
