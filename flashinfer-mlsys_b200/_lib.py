@@ -40,7 +40,9 @@ _lib = None
 
 
 def lib_path() -> str:
-    return _build.LIB_PATH
+    """The in-tree library, or the file named by MOE_FP8_DS_LIBRARY (an
+    alternative build of the same sources, e.g. for side-by-side timing)."""
+    return os.environ.get("MOE_FP8_DS_LIBRARY") or _build.LIB_PATH
 
 
 def load(build_if_missing: bool = True) -> ctypes.CDLL:
@@ -49,7 +51,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
     if _lib is not None:
         return _lib
     path = lib_path()
-    if not os.path.exists(path) or (build_if_missing and _build.is_stale()):
+    if path == _build.LIB_PATH and (not os.path.exists(path) or (build_if_missing and _build.is_stale())):
         if not build_if_missing:
             raise RuntimeError(f"{path} is missing: run `python -m` build (flashinfer-mlsys_b200/build.py)")
         _build.build()

@@ -18,6 +18,12 @@ namespace {
 constexpr int kRouteThreads = 256;      // 8 warps per CTA for multi-CTA routing
 constexpr int kRouteThreadsOne = 1024;  // a call with T <= 64 routes in one CTA of 32 warps
 constexpr int kOneCtaTokens = 64;
+// Cost of one extra work unit (its output stage and pipeline refill) in K
+// blocks, used when choosing the K split.
+#ifndef MOE_SPLIT_UNIT_OVERHEAD
+#define MOE_SPLIT_UNIT_OVERHEAD 16
+#endif
+constexpr int kSplitUnitOverhead = MOE_SPLIT_UNIT_OVERHEAD;
 
 // Sort 8 composite keys descending (19-comparator network, all-0/1-input verified).
 __device__ __forceinline__ void cmpswap(uint64_t& a, uint64_t& b) {
@@ -201,7 +207,7 @@ __global__ void __launch_bounds__(kRouteThreadsOne) route_plan_kernel(RouteArgs 
     auto cost = [&](int tiles, int nkb, int smax, int sp) -> long long {
       if (sp > smax || tiles <= 0) return 0x7fffffffffffLL;
       const long long units = (long long)tiles * sp;
-      return ((units + kSMs - 1) / kSMs) * ((nkb + sp - 1) / sp + 3);
+      return ((units + kSMs - 1) / kSMs) * ((nkb + sp - 1) / sp + kSplitUnitOverhead);
     };
     const int sp = lane + 1;
     const long long c1 = (total <= kMaxSplitMTiles) ? cost(total * kNT1, kKB1, 14, sp) : (sp == 1 ? 0 : 0x7fffffffffffLL);
