@@ -31,23 +31,32 @@ constexpr int kGemm1NBlocks = kGemm1N / kBlk; // 32
 //   B operand = expert weight rows (N = 256 per tile, two 128-row slabs)
 //   K step    = one 128-wide quantisation block per pipeline stage
 // GEMM1: N tile = 128 gate rows + the matching 128 up rows -> 16 N tiles,
-//        56 K blocks. GEMM2: N tile = 256 rows of W2 -> 28 N tiles,
-//        32 virtual K blocks (16 "hi" blocks + 16 "lo" blocks of the
-//        two-term FP8 intermediate, both against the same W2 block).
+//        56 K blocks, stage = A (128 token rows) + B (2 x 128 weight rows).
+// GEMM2: N tile = 256 rows of W2 -> 28 N tiles, 16 K blocks; the two-term
+//        e4m3 intermediate (hi and lo halves of every row, same block scale)
+//        is contracted as two A tiles against the same B tile into ONE TMEM
+//        partial, so a stage = A_hi + A_lo + B.
 // ---------------------------------------------------------------------------
 constexpr int kTileM = 128;
 constexpr int kTileN = 256;
 constexpr int kNT1 = kInter / kBlk;           // 16
 constexpr int kNT2 = kHidden / kTileN;        // 28
 constexpr int kKB1 = kHiddenBlocks;           // 56
-constexpr int kKB2 = 2 * kInterBlocks;        // 32
+constexpr int kKB2 = kInterBlocks;            // 16
 constexpr int kInterCols = 2 * kInter;        // 4096 bytes per intermediate row (hi | lo)
-constexpr float kLoScale = 0.0625f;           // lo term scale = hi scale / 16
 
-constexpr int kStages = 4;
-constexpr int kStageA = kTileM * kBlk;        // 16 KB of e4m3
+constexpr int kStageA = kTileM * kBlk;        // 16 KB of e4m3 (one A tile)
 constexpr int kStageB = kTileN * kBlk;        // 32 KB of e4m3
-constexpr int kStageBytes = kStageA + kStageB;
+template <int kMode>
+struct GemmCfg {
+  static constexpr int kATiles = (kMode == 1) ? 1 : 2;          // GEMM2: hi and lo
+  static constexpr int kStageBytes = kATiles * kStageA + kStageB;  // 48 KB / 64 KB
+  static constexpr int kStages = (kMode == 1) ? 4 : 3;          // 192 KB either way
+  static constexpr int kNKB = (kMode == 1) ? kKB1 : kKB2;
+  static constexpr int kNT = (kMode == 1) ? kNT1 : kNT2;
+};
+constexpr int kMaxStages = 4;
+constexpr int kRingBytes = 4 * (kStageA + kStageB);            // 192 KB for both GEMMs
 
 constexpr int kGemmThreads = 608;             // 19 warps
 constexpr int kScaleWarp = 2;                 // warp 2 streams block scales into shared memory

@@ -4,11 +4,12 @@
 //     (e4m3, 128x128 scales), K = 7168, then SwiGLU (ref_moe.py:153-159:
 //     C = G[:, :2048] * silu(G[:, 2048:]), silu(x) = x / (1 + exp(-x))) and
 //     re-quantisation of C into a two-term e4m3 intermediate per 1x128 block:
-//     hi = e4m3(C / s), lo = e4m3((C / s - hi) * 16), s = amax / 448, so
-//     C ~= s * hi + (s / 16) * lo.
-//   GEMM2 (kMode = 2): O[r, :] = Inter[r, :] x W2[e]^T over 32 virtual K
-//     blocks (16 hi + 16 lo, both against the same W2 block), then
-//     accum[token(r), :] += routing_weight(r) * O[r, :]  (ref_moe.py:162-166).
+//     hi = e4m3(C / s), lo = e4m3(C / s - hi), s = amax / 448, so
+//     C ~= s * (hi + lo).
+//   GEMM2 (kMode = 2): O[r, :] = (hi + lo)[r, :] x W2[e]^T over 16 K blocks:
+//     per block the hi and lo tiles are both multiplied against the same W2
+//     tile into one TMEM partial (they share the scale s), then
+//     out_rows[r, :] = routing_weight(r) * O[r, :]  (ref_moe.py:162-166).
 //
 // Warp roles (576 threads, one CTA per SM):
 //   warp 0      TMA producer (one elected lane): A tile 128x128 + two B slabs
@@ -57,8 +58,8 @@ struct Unit {
 
 template <int kMode>
 __device__ __forceinline__ Unit decode_unit(int u, int split, const int* prefix, const int* count, int e_local) {
-  constexpr int NT = (kMode == 1) ? kNT1 : kNT2;
-  constexpr int NKB = (kMode == 1) ? kKB1 : kKB2;
+  constexpr int NT = GemmCfg<kMode>::kNT;
+  constexpr int NKB = GemmCfg<kMode>::kNKB;
   Unit x;
   const int ks = u % split;
   const int tile = u / split;
@@ -87,8 +88,8 @@ struct __align__(16) SmemCtl {
   ScaleSlot scales[kScaleSlots];
   uint64_t sfull[kScaleSlots];
   uint64_t sempty[kScaleSlots];
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t mma_done;
@@ -163,7 +164,7 @@ __device__ __forceinline__ void swiglu_quant_store(const float* gate, const floa
       const float u0 = c[i + j] * inv, u1 = c[i + j + 1] * inv;
       const uint16_t h = f2_to_e4m3x2(u0, u1);
       const float q0 = e4m3_byte_to_f32(h & 0xFFu), q1 = e4m3_byte_to_f32(h >> 8);
-      const uint16_t l = f2_to_e4m3x2((u0 - q0) * 16.0f, (u1 - q1) * 16.0f);
+      const uint16_t l = f2_to_e4m3x2(u0 - q0, u1 - q1);
       hw |= static_cast<uint32_t>(h) << (8 * j);
       lw |= static_cast<uint32_t>(l) << (8 * j);
     }
@@ -184,12 +185,16 @@ template <int kMode>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                     GemmArgs p) {
-  constexpr int NT = (kMode == 1) ? kNT1 : kNT2;
+  using Cfg = GemmCfg<kMode>;
+  constexpr int NT = Cfg::kNT;
+  constexpr int kStages = Cfg::kStages;
+  constexpr int kStageBytes = Cfg::kStageBytes;
+  constexpr int kBOff = Cfg::kATiles * kStageA;  // B tile offset inside a stage
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment (in the shared window) for the 128-byte-swizzled tiles
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* tiles = smem;
-  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem + kStages * kStageBytes);
+  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem + kRingBytes);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -226,7 +231,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int u = blockIdx.x; u < units0 && n_pre < kStages; u += gridDim.x) {
       const Unit x = decode_unit<kMode>(u, split0, p.plan->mtile_prefix, p.plan->count, E_l);
       for (int kb = x.kb0; kb < x.kb1 && n_pre < kStages; ++kb, ++n_pre) {
-        uint8_t* sb = tiles + n_pre * kStageBytes + kStageA;
+        uint8_t* sb = tiles + n_pre * kStageBytes + kBOff;
         mbar_arrive_expect_tx(&ctl->full[n_pre], kStageBytes);
         if (kMode == 1) {
           const int y0 = x.e * kGemm1N + x.n * kBlk;
@@ -234,9 +239,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tma_load_2d(sb + kStageA, &map_w, kb * kBlk, y0 + kInter, &ctl->full[n_pre]);
         } else {
           const int y0 = x.e * kHidden + x.n * kTileN;
-          const int kx = (kb % kInterBlocks) * kBlk;
-          tma_load_2d(sb, &map_w, kx, y0, &ctl->full[n_pre]);
-          tma_load_2d(sb + kStageA, &map_w, kx, y0 + kBlk, &ctl->full[n_pre]);
+          tma_load_2d(sb, &map_w, kb * kBlk, y0, &ctl->full[n_pre]);
+          tma_load_2d(sb + kStageA, &map_w, kb * kBlk, y0 + kBlk, &ctl->full[n_pre]);
         }
       }
     }
@@ -270,32 +274,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1u;
           uint8_t* sa = tiles + s * kStageBytes;
-          uint8_t* sb = sa + kStageA;
-          if (static_cast<int>(it) < n_pre) {
-            // weights of this stage are already in flight: add the token tile
-            tma_load_2d(sa, &map_a, kb * kBlk, x.gm * kTileM, &ctl->full[s]);
-            continue;
+          uint8_t* sb = sa + kBOff;
+          if (static_cast<int>(it) >= n_pre) {
+            if (!mbar_wait_bounded(&ctl->empty[s], ph ^ 1u, kWaitLimitNs)) { signal_abort(ctl, p.status); break; }
+            mbar_arrive_expect_tx(&ctl->full[s], kStageBytes);
+            if (kMode == 1) {
+              const int y0 = x.e * kGemm1N + x.n * kBlk;
+              tma_load_2d(sb, &map_w, kb * kBlk, y0, &ctl->full[s]);
+              tma_load_2d(sb + kStageA, &map_w, kb * kBlk, y0 + kInter, &ctl->full[s]);
+            } else {
+              const int y0 = x.e * kHidden + x.n * kTileN;
+              tma_load_2d(sb, &map_w, kb * kBlk, y0, &ctl->full[s]);
+              tma_load_2d(sb + kStageA, &map_w, kb * kBlk, y0 + kBlk, &ctl->full[s]);
+            }
           }
-          if (!mbar_wait_bounded(&ctl->empty[s], ph ^ 1u, kWaitLimitNs)) { signal_abort(ctl, p.status); break; }
-          mbar_arrive_expect_tx(&ctl->full[s], kStageBytes);
+          // token tile(s); the weights of a prefetched stage are already in flight
           tma_load_2d(sa, &map_a, kb * kBlk, x.gm * kTileM, &ctl->full[s]);
-          if (kMode == 1) {
-            const int y0 = x.e * kGemm1N + x.n * kBlk;
-            tma_load_2d(sb, &map_w, kb * kBlk, y0, &ctl->full[s]);
-            tma_load_2d(sb + kStageA, &map_w, kb * kBlk, y0 + kInter, &ctl->full[s]);
-          } else {
-            const int y0 = x.e * kHidden + x.n * kTileN;
-            const int kx = (kb % kInterBlocks) * kBlk;
-            tma_load_2d(sb, &map_w, kx, y0, &ctl->full[s]);
-            tma_load_2d(sb + kStageA, &map_w, kx, y0 + kBlk, &ctl->full[s]);
-          }
+          if (kMode == 2) tma_load_2d(sa + kStageA, &map_a, kInter + kb * kBlk, x.gm * kTileM, &ctl->full[s]);
         }
         if (aborted(ctl)) break;
       }
       if (aborted(ctl)) {
         // drain: wait (bounded) for the loads this thread may still have in flight
         const uint32_t n_issued = it;
-        for (uint32_t j = (n_issued > kStages ? n_issued - kStages : 0); j < n_issued; ++j)
+        for (uint32_t j = (n_issued > (uint32_t)kStages ? n_issued - kStages : 0); j < n_issued; ++j)
           mbar_wait_bounded(&ctl->full[j % kStages], (j / kStages) & 1u, kWaitLimitNs);
       }
     }
@@ -320,12 +322,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           tc_fence_after();
           const uint32_t sa = smem_u32(tiles + s * kStageBytes);
-          const uint32_t sb = sa + kStageA;
-          const uint64_t da = smem_desc_sw128(sa), db = smem_desc_sw128(sb);
+          const uint32_t sb = sa + kBOff;
+          const uint64_t db = smem_desc_sw128(sb);
 #pragma unroll
-          for (int k = 0; k < kBlk / 32; ++k) {
-            // advance 32 bytes (one K=32 slice) inside the swizzle atom
-            mma_f8f6f4(tmem + buf * kTileN, da + 2 * k, db + 2 * k, idesc, k > 0 ? 1u : 0u);
+          for (int a = 0; a < Cfg::kATiles; ++a) {
+            const uint64_t da = smem_desc_sw128(sa + a * kStageA);
+#pragma unroll
+            for (int k = 0; k < kBlk / 32; ++k) {
+              // advance 32 bytes (one K=32 slice) inside the swizzle atom
+              mma_f8f6f4(tmem + buf * kTileN, da + 2 * k, db + 2 * k, idesc, (a > 0 || k > 0) ? 1u : 0u);
+            }
           }
           issued_any = true;
           mma_commit(&ctl->empty[s]);
@@ -353,7 +359,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         ScaleSlot* sl = &ctl->scales[j];
-        const int ka = (kMode == 1) ? kb : (kb % kInterBlocks);
+        const int ka = kb;
         cp_async_16(&sl->a[4 * lane], p.a_scale + (size_t)ka * p.rows_cap + (size_t)x.gm * kTileM + 4 * lane);
         if (lane < 2) {
           const float* src;
@@ -401,7 +407,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             f0 = as * sl->w[0];
             f1 = as * sl->w[1];
           } else {
-            f0 = f1 = as * ((kb >= kInterBlocks) ? kLoScale : 1.0f) * sl->w[cg >> 1];
+            f0 = f1 = as * sl->w[cg >> 1];
           }
         }
         __syncwarp();
@@ -533,7 +539,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-size_t gemm_smem_bytes() { return kStages * kStageBytes + sizeof(SmemCtl) + 1024; }
+size_t gemm_smem_bytes() { return kRingBytes + sizeof(SmemCtl) + 1024; }
 
 template <int kMode>
 cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,

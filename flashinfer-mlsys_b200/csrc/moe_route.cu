@@ -16,8 +16,8 @@ namespace moe {
 namespace {
 
 constexpr int kRouteThreads = 256;      // 8 warps per CTA for multi-CTA routing
-constexpr int kRouteThreadsOne = 1024;  // a call with T <= 64 routes in one CTA of 32 warps
-constexpr int kOneCtaTokens = 64;
+constexpr int kRouteThreadsOne = 1024;  // a call with T <= 32 routes in one CTA of 32 warps (one token each)
+constexpr int kOneCtaTokens = 32;
 // Cost of one extra work unit (its output stage and pipeline refill) in K
 // blocks, used when choosing the K split.
 #ifndef MOE_SPLIT_UNIT_OVERHEAD
@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(kRouteThreadsOne) route_plan_kernel(RouteArgs 
     };
     const int sp = lane + 1;
     const long long c1 = (total <= kMaxSplitMTiles) ? cost(total * kNT1, kKB1, 14, sp) : (sp == 1 ? 0 : 0x7fffffffffffLL);
-    const long long c2 = (total <= kMaxSplitMTiles) ? cost(total * kNT2, kKB2, 8, sp) : (sp == 1 ? 0 : 0x7fffffffffffLL);
+    const long long c2 = (total <= kMaxSplitMTiles) ? cost(total * kNT2, kKB2, 4, sp) : (sp == 1 ? 0 : 0x7fffffffffffLL);
     // pack (cost, split) so that the minimum prefers the smaller split on ties
     unsigned long long k1 = (static_cast<unsigned long long>(c1) << 8) | sp;
     unsigned long long k2 = (static_cast<unsigned long long>(c2) << 8) | sp;
@@ -355,7 +355,7 @@ int device_sm_count() {
 }
 
 int tokens_per_cta_for(int T) {
-  // T <= 64: one CTA of 32 warps; otherwise at most ~kSMs CTAs of 8 warps
+  // T <= 32: one CTA of 32 warps; otherwise at most ~kSMs CTAs of 8 warps
   if (T <= kOneCtaTokens) return kOneCtaTokens;
   int per = (T + kSMs - 1) / kSMs;
   per = ((per + 7) / 8) * 8;
