@@ -48,6 +48,7 @@ struct GemmArgs {
   float* g2_part;           // GEMM2 split-K scratch: [kMaxSplitMTiles*128][7168]
   int32_t* tile_sem2;       // GEMM2 split-K counters: [kMaxSplitMTiles][28]
   unsigned* status;
+  int plan_early;           // 1: the plan was complete before the previous kernel released this one
 };
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: only reached if something is broken
@@ -97,6 +98,8 @@ struct __align__(16) SmemCtl {
   uint32_t tmem_base;
   int abort_flag;
   int fixup_flag;
+  int plan_total;      // total m-tiles of the call
+  int plan_split;      // K split of this GEMM
   int prefix[kExperts + 1];
   int count[kExperts];
   float amax[4][kTileM];
@@ -220,16 +223,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tensormap(&map_a);
     prefetch_tensormap(&map_w);
   }
-  // Weight tiles do not depend on the previous kernel: the producer issues
-  // the B (weight) loads of its first stages before waiting for it. The plan
-  // is already complete here (it was written by the routing kernel, which
-  // finished before the previous kernel released this one).
+  if (warp == 1) {
+    tmem_alloc(&ctl->tmem_base, 512);
+    tmem_relinquish();
+  }
+  // The device plan (per-expert rows, m-tile prefix, K split) goes to shared
+  // memory in one pass. When it was complete before this kernel was released
+  // (it is written by the routing kernel, at least two kernels back), that
+  // happens before waiting for the previous kernel, and so does the issue of
+  // the first stages' weight tiles, which depend on nothing produced there.
+  auto load_plan = [&]() {
+    for (int e = tid; e <= E_l; e += blockDim.x) ctl->prefix[e] = p.plan->mtile_prefix[e];
+    for (int e = tid; e < E_l; e += blockDim.x) ctl->count[e] = p.plan->count[e];
+    if (tid == 0) {
+      ctl->plan_total = p.plan->total_mtiles;
+      ctl->plan_split = (kMode == 1) ? p.plan->split1 : p.plan->split2;
+    }
+  };
+  if (p.plan_early) load_plan();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   int n_pre = 0;
-  if (tid == 0) {
-    const int units0 = p.plan->total_mtiles * NT * ((kMode == 1) ? p.plan->split1 : p.plan->split2);
-    const int split0 = (kMode == 1) ? p.plan->split1 : p.plan->split2;
+  if (p.plan_early && tid == 0) {
+    const int split0 = ctl->plan_split;
+    const int units0 = ctl->plan_total * NT * split0;
     for (int u = blockIdx.x; u < units0 && n_pre < kStages; u += gridDim.x) {
-      const Unit x = decode_unit<kMode>(u, split0, p.plan->mtile_prefix, p.plan->count, E_l);
+      const Unit x = decode_unit<kMode>(u, split0, ctl->prefix, ctl->count, E_l);
       for (int kb = x.kb0; kb < x.kb1 && n_pre < kStages; ++kb, ++n_pre) {
         uint8_t* sb = tiles + n_pre * kStageBytes + kBOff;
         mbar_arrive_expect_tx(&ctl->full[n_pre], kStageBytes);
@@ -245,22 +265,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   }
-  if (warp == 1) {
-    tmem_alloc(&ctl->tmem_base, 512);
-    tmem_relinquish();
-  }
-  // everything above overlaps the previous kernel's tail; from here on we
-  // read what it produced
+  // from here on we read what the previous kernel produced
   griddep_wait();
   griddep_launch_dependents();
-  for (int e = tid; e <= E_l; e += blockDim.x) ctl->prefix[e] = p.plan->mtile_prefix[e];
-  for (int e = tid; e < E_l; e += blockDim.x) ctl->count[e] = p.plan->count[e];
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+  if (!p.plan_early) {
+    load_plan();
+    __syncthreads();
+  }
 
-  const int total_mtiles = p.plan->total_mtiles;
-  const int split = (kMode == 1) ? p.plan->split1 : p.plan->split2;
+  const int total_mtiles = ctl->plan_total;
+  const int split = ctl->plan_split;
   const int units = total_mtiles * NT * split;
   const uint32_t tmem = ctl->tmem_base;
 
@@ -543,7 +557,7 @@ size_t gemm_smem_bytes() { return kRingBytes + sizeof(SmemCtl) + 1024; }
 
 template <int kMode>
 cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
-                        const float* w_scale, cudaStream_t s) {
+                        const float* w_scale, cudaStream_t s, int plan_early) {
   static int configured[2] = {0, 0};
   const size_t smem = gemm_smem_bytes();
   if (!configured[kMode - 1]) {
@@ -568,6 +582,7 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
   p.g2_part = ws.g2_part;
   p.tile_sem2 = ws.tile_sem2;
   p.status = ws.status;
+  p.plan_early = plan_early;
   return launch_k(moe_gemm_kernel<kMode>, dim3(sms), dim3(kGemmThreads), smem, s, true, map_a, map_w, p);
 }
 
@@ -575,12 +590,13 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
 
 cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
                          const float* w_scale, cudaStream_t s) {
-  return launch_gemm<1>(ws, map_a, map_w, w_scale, s);
+  // the permutation kernel runs between the routing kernel and GEMM1
+  return launch_gemm<1>(ws, map_a, map_w, w_scale, s, 1);
 }
 
 cudaError_t launch_gemm2(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
                          const float* w_scale, cudaStream_t s) {
-  return launch_gemm<2>(ws, map_a, map_w, w_scale, s);
+  return launch_gemm<2>(ws, map_a, map_w, w_scale, s, 1);
 }
 
 }  // namespace moe

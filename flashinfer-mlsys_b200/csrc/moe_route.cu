@@ -15,9 +15,8 @@ namespace moe {
 
 namespace {
 
-constexpr int kRouteThreads = 256;      // 8 warps per CTA for multi-CTA routing
-constexpr int kRouteThreadsOne = 1024;  // a call with T <= 32 routes in one CTA of 32 warps (one token each)
-constexpr int kOneCtaTokens = 32;
+constexpr int kRouteThreads = 256;  // 8 warps, one token per warp at a time
+constexpr int kMinTokensPerCta = 8;
 // Cost of one extra work unit (its output stage and pipeline refill) in K
 // blocks, used when choosing the K split.
 #ifndef MOE_SPLIT_UNIT_OVERHEAD
@@ -40,7 +39,67 @@ __device__ __forceinline__ void sort8_desc(uint64_t (&c)[8]) {
   cmpswap(c[1], c[2]); cmpswap(c[3], c[4]); cmpswap(c[5], c[6]);
 }
 
-__global__ void __launch_bounds__(kRouteThreadsOne) route_plan_kernel(RouteArgs a, Workspace ws) {
+// One warp, one token: copy the e4m3 row (7168 B) and its 56 block scales to
+// every local expert slot the token was routed to, and record the token's
+// rows. `prefix` is the m-tile prefix of the local experts.
+__device__ __forceinline__ void permute_token(int t, int lane, const uint8_t* __restrict__ hidden,
+                                              const float* __restrict__ hidden_scale, int T, int offset,
+                                              int tokens_per_cta, const int* prefix, const Workspace& ws) {
+  const int E_l = ws.e_local;
+  int row = -1;
+  float w = 0.f;
+  if (lane < kTopK) {
+    const size_t o = (size_t)t * kTopK + lane;
+    const int r = ws.topk_rank[o];
+    if (r >= 0) {
+      const int le = ws.topk_ids[o] - offset;
+      const int cta = t / tokens_per_cta;
+      row = prefix[le] * kTileM + ws.cta_off[(size_t)cta * E_l + le] + r;
+      w = ws.topk_w[o];
+    }
+  }
+  // token_rows[t]: this token's rows in ascending expert id (the order in which
+  // ref_moe.py:134-166 accumulates the experts), -1 padded
+  {
+    const int my_e = (row >= 0) ? ws.topk_ids[(size_t)t * kTopK + lane] : 0x7fffffff;
+    int rank = 0, n_loc = 0;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      const int ek = __shfl_sync(0xffffffffu, my_e, k);
+      const int rk = __shfl_sync(0xffffffffu, row, k);
+      rank += (rk >= 0 && (ek < my_e || (ek == my_e && k < lane))) ? 1 : 0;
+      n_loc += (rk >= 0) ? 1 : 0;
+    }
+    if (lane < kTopK) {
+      if (row >= 0) ws.token_rows[(size_t)t * kTopK + rank] = row;
+      if (lane >= n_loc) ws.token_rows[(size_t)t * kTopK + lane] = -1;
+    }
+  }
+  const unsigned has = __ballot_sync(0xffffffffu, row >= 0);
+  if (!has) return;
+  const uint4* src = reinterpret_cast<const uint4*>(hidden + (size_t)t * kHidden);
+  const float sc0 = __ldg(hidden_scale + (size_t)lane * T + t);
+  const float sc1 = (lane + 32 < kHiddenBlocks) ? __ldg(hidden_scale + (size_t)(lane + 32) * T + t) : 0.f;
+  unsigned m = has;
+  while (m) {
+    const int k = __ffs(m) - 1;
+    m &= m - 1;
+    const int r = __shfl_sync(0xffffffffu, row, k);
+    const float wk = __shfl_sync(0xffffffffu, w, k);
+    // 14 chunks of 16 B per lane; repeated destinations re-read the row from L1
+    uint4* dst = reinterpret_cast<uint4*>(ws.a1 + (size_t)r * kHidden);
+#pragma unroll 7
+    for (int i = 0; i < kHidden / 16 / 32; ++i) dst[lane + 32 * i] = __ldg(src + lane + 32 * i);
+    ws.a1_scale[(size_t)lane * ws.rows_cap + r] = sc0;
+    if (lane + 32 < kHiddenBlocks) ws.a1_scale[(size_t)(lane + 32) * ws.rows_cap + r] = sc1;
+    if (lane == 0) {
+      ws.row_token[r] = t;
+      ws.row_weight[r] = wk;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, Workspace ws) {
   __shared__ int hist[kExperts];
   __shared__ int is_last;
   const int tid = threadIdx.x;
@@ -178,7 +237,7 @@ __global__ void __launch_bounds__(kRouteThreadsOne) route_plan_kernel(RouteArgs 
     if (tid < E_l) c = atomicExch(&ws.expert_fill[tid], 0);  // read and reset for the next call
   }
   // ---- m-tile prefix and K-split plan ----
-  __shared__ int warp_tot[2][kRouteThreadsOne / 32];
+  __shared__ int warp_tot[2][kRouteThreads / 32];
   if (tid < E_l) {
     ws.plan->count[tid] = c;
     if (a.user_counts) a.user_counts[tid] = c;
@@ -233,68 +292,13 @@ __global__ void __launch_bounds__(kRouteThreadsOne) route_plan_kernel(RouteArgs 
   }
 }
 
-// One warp per token: copy the e4m3 row (7168 B) and its 56 block scales to
-// every local expert slot the token was routed to.
 __global__ void __launch_bounds__(256) permute_kernel(PermuteArgs a, Workspace ws) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + warp;
   griddep_wait();
   griddep_launch_dependents();
   if (t >= a.T) return;
-  const int E_l = ws.e_local;
-  int row = -1;
-  float w = 0.f;
-  if (lane < kTopK) {
-    const size_t o = (size_t)t * kTopK + lane;
-    const int r = ws.topk_rank[o];
-    if (r >= 0) {
-      const int le = ws.topk_ids[o] - a.offset;
-      const int cta = t / a.tokens_per_cta;
-      row = ws.plan->mtile_prefix[le] * kTileM + ws.cta_off[(size_t)cta * E_l + le] + r;
-      w = ws.topk_w[o];
-    }
-  }
-  // token_rows[t]: this token's rows in ascending expert id (the order in which
-  // ref_moe.py:134-166 accumulates the experts), -1 padded
-  {
-    const int my_e = (row >= 0) ? ws.topk_ids[(size_t)t * kTopK + lane] : 0x7fffffff;
-    int rank = 0, n_loc = 0;
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-      const int ek = __shfl_sync(0xffffffffu, my_e, k);
-      const int rk = __shfl_sync(0xffffffffu, row, k);
-      rank += (rk >= 0 && (ek < my_e || (ek == my_e && k < lane))) ? 1 : 0;
-      n_loc += (rk >= 0) ? 1 : 0;
-    }
-    if (lane < kTopK) {
-      if (row >= 0) ws.token_rows[(size_t)t * kTopK + rank] = row;
-      if (lane >= n_loc) ws.token_rows[(size_t)t * kTopK + lane] = -1;
-    }
-  }
-  const unsigned has = __ballot_sync(0xffffffffu, row >= 0);
-  if (!has) return;
-  const uint4* src = reinterpret_cast<const uint4*>(a.hidden + (size_t)t * kHidden);
-  uint4 v[kHidden / 16 / 32];  // 14 chunks of 16 B per lane
-#pragma unroll
-  for (int i = 0; i < kHidden / 16 / 32; ++i) v[i] = __ldg(src + lane + 32 * i);
-  const float sc0 = __ldg(a.hidden_scale + (size_t)lane * a.T + t);
-  const float sc1 = (lane + 32 < kHiddenBlocks) ? __ldg(a.hidden_scale + (size_t)(lane + 32) * a.T + t) : 0.f;
-  unsigned m = has;
-  while (m) {
-    const int k = __ffs(m) - 1;
-    m &= m - 1;
-    const int r = __shfl_sync(0xffffffffu, row, k);
-    const float wk = __shfl_sync(0xffffffffu, w, k);
-    uint4* dst = reinterpret_cast<uint4*>(ws.a1 + (size_t)r * kHidden);
-#pragma unroll
-    for (int i = 0; i < kHidden / 16 / 32; ++i) dst[lane + 32 * i] = v[i];
-    ws.a1_scale[(size_t)lane * ws.rows_cap + r] = sc0;
-    if (lane + 32 < kHiddenBlocks) ws.a1_scale[(size_t)(lane + 32) * ws.rows_cap + r] = sc1;
-    if (lane == 0) {
-      ws.row_token[r] = t;
-      ws.row_weight[r] = wk;
-    }
-  }
+  permute_token(t, lane, a.hidden, a.hidden_scale, a.T, a.offset, a.tokens_per_cta, ws.plan->mtile_prefix, ws);
 }
 
 // out[t, :] = sum over the token's local rows (ascending expert id) of the
@@ -355,11 +359,11 @@ int device_sm_count() {
 }
 
 int tokens_per_cta_for(int T) {
-  // T <= 32: one CTA of 32 warps; otherwise at most ~kSMs CTAs of 8 warps
-  if (T <= kOneCtaTokens) return kOneCtaTokens;
+  // one token per warp for small T (a call with T <= 8 is a single CTA and
+  // needs no cross-CTA handshake); at most ~kSMs routing CTAs for large T
   int per = (T + kSMs - 1) / kSMs;
   per = ((per + 7) / 8) * 8;
-  return per < 8 ? 8 : per;
+  return per < kMinTokensPerCta ? kMinTokensPerCta : per;
 }
 
 int route_ctas_for(int T) {
@@ -370,8 +374,7 @@ int route_ctas_for(int T) {
 
 cudaError_t launch_route(const Workspace& ws, const RouteArgs& a, cudaStream_t s) {
   const int grid = route_ctas_for(a.T);
-  const int threads = (grid == 1) ? kRouteThreadsOne : kRouteThreads;
-  return launch_k(route_plan_kernel, dim3(grid), dim3(threads), 0, s, false, a, ws);
+  return launch_k(route_plan_kernel, dim3(grid), dim3(kRouteThreads), 0, s, false, a, ws);
 }
 
 cudaError_t launch_permute(const Workspace& ws, const PermuteArgs& a, cudaStream_t s) {
