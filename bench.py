@@ -503,12 +503,68 @@ def bench_ep(args):
         dist.destroy_process_group()
 
 
+def bench_flashinfer(args):
+    """Comparator (not the reference): FlashInfer's fused FP8 block-scale MoE,
+    flashinfer.fused_moe.trtllm_fp8_block_scale_moe, called as a library on
+    the same inputs, with DeepSeek-V3 routing (routing_method_type=2). The
+    reference wires this call in solution/triton/dsl-temp1.py:226-263. Its
+    first call JIT-compiles the launcher (minutes on a fresh machine); the
+    line also reports its parity against the CPU oracle on the first T."""
+    import numpy as np
+    import torch
+    from flashinfer.fused_moe import trtllm_fp8_block_scale_moe
+
+    dev = torch.device("cuda", 0)
+    wl = importlib.import_module("flashinfer-mlsys_b200.workloads")
+    O = importlib.import_module("oracle.moe_oracle")
+    Ts, wdesc = WORKLOADS[args.workload if args.workload != "ep" else "decode_sweep"]
+    if args.T:
+        Ts = tuple(int(t) for t in args.T.split(","))
+    w = wl.make_weights(32, 0, dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    per_T, parity = {}, None
+    for T in Ts:
+        acts = wl.config_activations(T)
+        a = acts.to(dev)
+
+        def fn():
+            return trtllm_fp8_block_scale_moe(a.logits, a.bias, a.hidden, a.hidden_scale, w.w13, w.s13, w.w2, w.s2,
+                                              256, 8, 8, 4, 2048, 0, 32, 2.5, routing_method_type=2)
+
+        out = fn()
+        torch.cuda.synchronize()
+        if parity is None:
+            ref = O.moe_forward(acts.logits.numpy(), O.as_f32(acts.bias), O.as_u8(acts.hidden),
+                                acts.hidden_scale.numpy(), lambda le: w.expert_cpu(le), 0, 2.5, 32)
+            parity = {"T": T, "frac_within_1e-2": O.allclose_fraction(
+                out.float().cpu().numpy(), O.bf16_bits_to_f32(ref["out_bf16"]), 1e-2, 1e-2)}
+        for _ in range(args.warmup):
+            flush.zero_()
+            fn()
+        evs = []
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        per_T[str(T)] = round(statistics.mean(x.elapsed_time(y) for x, y in evs) * 1e3, 2)
+    value = statistics.mean(per_T.values())
+    print(json.dumps({"metric": METRIC, "value": round(value, 3), "unit": "us/call", "impl": "flashinfer",
+                      "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+                      "config": {"workload": f"{args.workload}: {wdesc}", "T": list(Ts)}, "sweep_us": per_T,
+                      "parity_vs_oracle": parity}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "flashinfer"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=None,
                     help="default: decode_sweep on 1 GPU, ep on N>1 GPUs")
     ap.add_argument("--T", default="", help="comma-separated token counts overriding the workload's sweep")
@@ -520,6 +576,8 @@ def main():
         args.workload = "ep" if world > 1 else "decode_sweep"
     if args.impl == "reference":
         bench_reference(args)
+    elif args.impl == "flashinfer":
+        bench_flashinfer(args)
     elif args.workload == "ep":
         bench_ep(args)
     else:
