@@ -41,34 +41,36 @@ EncodeTiledFn encode_fn() {
 struct MapKey {
   const void* base;
   uint64_t cols, rows;
+  uint32_t box_rows;
 };
 constexpr int kMapCache = 32;
 MapKey g_map_key[kMapCache];
 CUtensorMap g_map_val[kMapCache];
 int g_map_next = 0;
 
-bool encode_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows);
+bool encode_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows);
 
-bool make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows) {
+bool make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows = 128) {
   for (int i = 0; i < kMapCache; ++i) {
-    if (g_map_key[i].base == base && g_map_key[i].cols == cols && g_map_key[i].rows == rows && base) {
+    if (g_map_key[i].base == base && g_map_key[i].cols == cols && g_map_key[i].rows == rows &&
+        g_map_key[i].box_rows == box_rows && base) {
       *m = g_map_val[i];
       return true;
     }
   }
-  if (!encode_map(m, base, cols, rows)) return false;
-  g_map_key[g_map_next] = MapKey{base, cols, rows};
+  if (!encode_map(m, base, cols, rows, box_rows)) return false;
+  g_map_key[g_map_next] = MapKey{base, cols, rows, box_rows};
   g_map_val[g_map_next] = *m;
   g_map_next = (g_map_next + 1) % kMapCache;
   return true;
 }
 
-bool encode_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows) {
+bool encode_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {cols};
-  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t box[2] = {128, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -140,7 +142,7 @@ void forget_maps(const void* base, size_t bytes) {
   const uint8_t* b = static_cast<const uint8_t*>(base);
   for (int i = 0; i < kMapCache; ++i) {
     const uint8_t* k = static_cast<const uint8_t*>(g_map_key[i].base);
-    if (k >= b && k < b + bytes) g_map_key[i] = MapKey{nullptr, 0, 0};
+    if (k >= b && k < b + bytes) g_map_key[i] = MapKey{nullptr, 0, 0, 0};
   }
 }
 
@@ -251,10 +253,14 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
   if (launch_route(*ws, ra, s) != cudaSuccess) return MOE_ERR_CUDA;
   if (route_only) return MOE_OK;
 
+  // calls with at most 64 rows use the skinny GEMM configuration (64-row
+  // token tiles, one more stage of weights in flight)
+  const bool skinny = T <= kSkinnyMaxRows;
+  const uint32_t a_box = skinny ? kSkinnyMaxRows : kTileM;
   CUtensorMap ma1, mw1, ma2, mw2;
-  if (!make_map(&ma1, ws->a1, kHidden, ws->rows_cap) ||
+  if (!make_map(&ma1, ws->a1, kHidden, ws->rows_cap, a_box) ||
       !make_map(&mw1, w1, kHidden, static_cast<uint64_t>(E_l) * kGemm1N) ||
-      !make_map(&ma2, ws->inter, kInterCols, ws->rows_cap) ||
+      !make_map(&ma2, ws->inter, kInterCols, ws->rows_cap, a_box) ||
       !make_map(&mw2, w2, kInter, static_cast<uint64_t>(E_l) * kHidden))
     return MOE_ERR_CUDA;
 
@@ -267,9 +273,9 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
   prof_mark(1, s);
   if (launch_permute(*ws, pa, s) != cudaSuccess) return MOE_ERR_CUDA;
   prof_mark(2, s);
-  if (launch_gemm1(*ws, ma1, mw1, s1, s) != cudaSuccess) return MOE_ERR_CUDA;
+  if (launch_gemm1(*ws, ma1, mw1, s1, s, skinny) != cudaSuccess) return MOE_ERR_CUDA;
   prof_mark(3, s);
-  if (launch_gemm2(*ws, ma2, mw2, s2, s) != cudaSuccess) return MOE_ERR_CUDA;
+  if (launch_gemm2(*ws, ma2, mw2, s2, s, skinny) != cudaSuccess) return MOE_ERR_CUDA;
   prof_mark(4, s);
   if (launch_finalize(*ws, static_cast<int>(T), out, out_fp32, s) != cudaSuccess) return MOE_ERR_CUDA;
   prof_mark(5, s);

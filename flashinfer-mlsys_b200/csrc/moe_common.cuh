@@ -45,18 +45,26 @@ constexpr int kKB1 = kHiddenBlocks;           // 56
 constexpr int kKB2 = kInterBlocks;            // 16
 constexpr int kInterCols = 2 * kInter;        // 4096 bytes per intermediate row (hi | lo)
 
-constexpr int kStageA = kTileM * kBlk;        // 16 KB of e4m3 (one A tile)
+constexpr int kStageA = kTileM * kBlk;        // 16 KB of e4m3 (one 128-row A tile)
 constexpr int kStageB = kTileN * kBlk;        // 32 KB of e4m3
-template <int kMode>
+// kSkinny: calls with at most 64 tokens load 64-row token tiles (8 KB), which
+// leaves room for one more stage of weights in flight. The MMA still reads
+// 128 rows; rows 64-127 then see unrelated shared memory and only produce
+// accumulator rows that are never stored (every m-tile has <= 64 valid rows).
+template <int kMode, int kSkinny = 0>
 struct GemmCfg {
   static constexpr int kATiles = (kMode == 1) ? 1 : 2;          // GEMM2: hi and lo
-  static constexpr int kStageBytes = kATiles * kStageA + kStageB;  // 48 KB / 64 KB
-  static constexpr int kStages = (kMode == 1) ? 4 : 3;          // 192 KB either way
+  static constexpr int kARows = kSkinny ? 64 : kTileM;
+  static constexpr int kABytes = kARows * kBlk;                 // bytes loaded (and slot size) per A tile
+  static constexpr int kStageBytes = kATiles * kABytes + kStageB;
+  static constexpr int kStages = kSkinny ? ((kMode == 1) ? 5 : 4) : ((kMode == 1) ? 4 : 3);
+  static constexpr int kRing = kStages * kStageBytes;
   static constexpr int kNKB = (kMode == 1) ? kKB1 : kKB2;
   static constexpr int kNT = (kMode == 1) ? kNT1 : kNT2;
 };
-constexpr int kMaxStages = 4;
-constexpr int kRingBytes = 4 * (kStageA + kStageB);            // 192 KB for both GEMMs
+constexpr int kMaxStages = 5;
+constexpr int kRingBytes = 200 * 1024;          // >= kRing of every configuration
+constexpr int kSkinnyMaxRows = 64;
 
 constexpr int kGemmThreads = 608;             // 19 warps
 constexpr int kScaleWarp = 2;                 // warp 2 streams block scales into shared memory

@@ -184,15 +184,17 @@ __device__ __forceinline__ void swiglu_quant_store(const float* gate, const floa
   if (cg == 0) p.inter_scale[(size_t)n * p.rows_cap + row] = scale;
 }
 
-template <int kMode>
+template <int kMode, int kSkinny>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                     GemmArgs p) {
-  using Cfg = GemmCfg<kMode>;
+  using Cfg = GemmCfg<kMode, kSkinny>;
+  static_assert(Cfg::kRing <= kRingBytes && Cfg::kStages <= kMaxStages, "stage ring does not fit");
   constexpr int NT = Cfg::kNT;
   constexpr int kStages = Cfg::kStages;
   constexpr int kStageBytes = Cfg::kStageBytes;
-  constexpr int kBOff = Cfg::kATiles * kStageA;  // B tile offset inside a stage
+  constexpr int kABytes = Cfg::kABytes;
+  constexpr int kBOff = Cfg::kATiles * kABytes;  // B tile offset inside a stage
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment (in the shared window) for the 128-byte-swizzled tiles
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -304,7 +306,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           // token tile(s); the weights of a prefetched stage are already in flight
           tma_load_2d(sa, &map_a, kb * kBlk, x.gm * kTileM, &ctl->full[s]);
-          if (kMode == 2) tma_load_2d(sa + kStageA, &map_a, kInter + kb * kBlk, x.gm * kTileM, &ctl->full[s]);
+          if (kMode == 2) tma_load_2d(sa + kABytes, &map_a, kInter + kb * kBlk, x.gm * kTileM, &ctl->full[s]);
         }
         if (aborted(ctl)) break;
       }
@@ -340,7 +342,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint64_t db = smem_desc_sw128(sb);
 #pragma unroll
           for (int a = 0; a < Cfg::kATiles; ++a) {
-            const uint64_t da = smem_desc_sw128(sa + a * kStageA);
+            const uint64_t da = smem_desc_sw128(sa + a * kABytes);
 #pragma unroll
             for (int k = 0; k < kBlk / 32; ++k) {
               // advance 32 bytes (one K=32 slice) inside the swizzle atom
@@ -555,16 +557,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 size_t gemm_smem_bytes() { return kRingBytes + sizeof(SmemCtl) + 1024; }
 
-template <int kMode>
+template <int kMode, int kSkinny>
 cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
                         const float* w_scale, cudaStream_t s, int plan_early) {
-  static int configured[2] = {0, 0};
+  static int configured = 0;
   const size_t smem = gemm_smem_bytes();
-  if (!configured[kMode - 1]) {
-    cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<kMode>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<kMode, kSkinny>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    configured[kMode - 1] = 1;
+    configured = 1;
   }
   const int sms = device_sm_count();
   GemmArgs p{};
@@ -583,20 +585,23 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
   p.tile_sem2 = ws.tile_sem2;
   p.status = ws.status;
   p.plan_early = plan_early;
-  return launch_k(moe_gemm_kernel<kMode>, dim3(sms), dim3(kGemmThreads), smem, s, true, map_a, map_w, p);
+  return launch_k(moe_gemm_kernel<kMode, kSkinny>, dim3(sms), dim3(kGemmThreads), smem, s, true, map_a, map_w, p);
 }
 
 }  // namespace
 
+// The permutation kernel runs between the routing kernel and GEMM1, so both
+// GEMMs may read the plan before their programmatic-launch wait.
 cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
-                         const float* w_scale, cudaStream_t s) {
-  // the permutation kernel runs between the routing kernel and GEMM1
-  return launch_gemm<1>(ws, map_a, map_w, w_scale, s, 1);
+                         const float* w_scale, cudaStream_t s, bool skinny) {
+  return skinny ? launch_gemm<1, 1>(ws, map_a, map_w, w_scale, s, 1)
+                : launch_gemm<1, 0>(ws, map_a, map_w, w_scale, s, 1);
 }
 
 cudaError_t launch_gemm2(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
-                         const float* w_scale, cudaStream_t s) {
-  return launch_gemm<2>(ws, map_a, map_w, w_scale, s, 1);
+                         const float* w_scale, cudaStream_t s, bool skinny) {
+  return skinny ? launch_gemm<2, 1>(ws, map_a, map_w, w_scale, s, 1)
+                : launch_gemm<2, 0>(ws, map_a, map_w, w_scale, s, 1);
 }
 
 }  // namespace moe

@@ -89,10 +89,12 @@ int tokens_per_cta_for(int T);
 
 cudaError_t launch_route(const Workspace& ws, const RouteArgs& a, cudaStream_t s);
 cudaError_t launch_permute(const Workspace& ws, const PermuteArgs& a, cudaStream_t s);
+// skinny: every m-tile has at most kSkinnyMaxRows valid rows (map_a then has
+// kSkinnyMaxRows-row boxes)
 cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
-                         const float* w_scale, cudaStream_t s);
+                         const float* w_scale, cudaStream_t s, bool skinny);
 cudaError_t launch_gemm2(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
-                         const float* w_scale, cudaStream_t s);
+                         const float* w_scale, cudaStream_t s, bool skinny);
 cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32, cudaStream_t s);
 
 
