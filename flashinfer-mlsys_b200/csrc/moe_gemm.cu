@@ -126,6 +126,18 @@ struct EpiSync {
   }
 };
 
+// acc[i] += f * v[i] for 16 values, as eight packed f32x2 FMAs (each
+// component rounds exactly like fmaf).
+__device__ __forceinline__ void promote16(float* acc, const float (&v)[16], float f) {
+  const float2 ff = make_float2(f, f);
+#pragma unroll
+  for (int i = 0; i < 16; i += 2) {
+    const float2 r = __ffma2_rn(ff, make_float2(v[i], v[i + 1]), make_float2(acc[i], acc[i + 1]));
+    acc[i] = r.x;
+    acc[i + 1] = r.y;
+  }
+}
+
 __device__ __forceinline__ float silu_ref(float x) { return x / (1.0f + expf(-x)); }
 
 __device__ __forceinline__ float e4m3_byte_to_f32(uint32_t b) {
@@ -447,8 +459,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t col = (h < 2) ? c0 + 16 * h : c1 + 16 * (h - 2);
           const float f = (h < 2) ? f0 : f1;
           tmem_ld_32x32b_x16(tb + col, v);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) acc[16 * h + i] = fmaf(f, v[i], acc[16 * h + i]);
+          promote16(acc + 16 * h, v, f);
         }
         tc_fence_before();
         __syncwarp();
