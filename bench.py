@@ -184,13 +184,15 @@ def bench_ours(args):
     # per-kernel device times (CUDA events recorded by the library on this stream)
     lib.moe_fp8_ds_profile_enable(1)
     kern = {T: np.zeros(5) for T in Ts}
+    nkern = {T: 5 for T in Ts}  # 1 when the call is served by the fused decode kernel
     buf = (ctypes.c_float * 5)()
     for s in range(args.steps):
         for T in Ts:
             flush.zero_()
             call(T)
             n = lib.moe_fp8_ds_profile_last(buf, 5)
-            kern[T] += np.array(buf[:5])
+            nkern[T] = n
+            kern[T][:n] += np.array(buf[:n])
     lib.moe_fp8_ds_profile_enable(0)
     for T in Ts:
         kern[T] /= args.steps
@@ -236,6 +238,7 @@ def bench_ours(args):
     sweep = {}
     tot_flops = tot_bytes = 0
     g1_bytes = g1_ms = 0.0
+    fused_bytes = fused_ms = 0.0
     for T in Ts:
         st = stats[T]
         flops = wl.moe_flops(st["n_assign"])
@@ -247,18 +250,31 @@ def bench_ours(args):
             **st,
             "tflops": round(flops / (ms * 1e-3) / 1e12, 3), "gbs": round(byts / (ms * 1e-3) / 1e9, 1),
             "roofline_frac": round(t_roof_ms / ms, 4),
-            "kernel_us": {k: round(v * 1e3, 2) for k, v in zip(
-                ["route", "permute", "gemm1", "gemm2", "finalize"], kern[T])},
+            "kernel_us": ({"fused_decode": round(kern[T][0] * 1e3, 2)} if nkern[T] == 1 else
+                          {k: round(v * 1e3, 2) for k, v in zip(
+                              ["route", "permute", "gemm1", "gemm2", "finalize"], kern[T])}),
         }
         tot_flops += flops
         tot_bytes += byts
         # GEMM1 algorithmic bytes: touched W13 + scales, permuted rows in, intermediate out
-        g1_bytes += st["e_touched"] * (4096 * 7168 + 32 * 56 * 4) + st["n_assign"] * (7168 + 56 * 4 + 4096 + 64)
-        g1_ms += kern[T][2]
+        if nkern[T] == 1:
+            # fused decode kernel: the whole layer's algorithmic bytes
+            fused_bytes += byts
+            fused_ms += kern[T][0]
+        else:
+            g1_bytes += st["e_touched"] * (4096 * 7168 + 32 * 56 * 4) + st["n_assign"] * (7168 + 56 * 4 + 4096 + 64)
+            g1_ms += kern[T][2]
     tot_ms = sum(per_T_ms.values())
     n_calls = len(Ts)
     value = tot_ms * 1e3 / n_calls
-    achieved = g1_bytes / (g1_ms * 1e-3) / 1e9 if g1_ms > 0 else 0.0
+    if fused_ms > 0 and fused_ms >= g1_ms:
+        roof_kernel = "moe_decode_kernel (whole layer in one launch)"
+        achieved = fused_bytes / (fused_ms * 1e-3) / 1e9
+        traffic = _ncu_traffic("decode_dram_bytes_per_launch")
+    else:
+        roof_kernel = "moe_gemm_kernel<1> (GEMM1 + SwiGLU)"
+        achieved = g1_bytes / (g1_ms * 1e-3) / 1e9 if g1_ms > 0 else 0.0
+        traffic = _ncu_traffic("gemm1_dram_bytes_per_launch")
     clocks = clk.summary()
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "us/call", "n_gpus": world, "steps": args.steps,
@@ -272,12 +288,12 @@ def bench_ours(args):
         "tflops": round(tot_flops / (tot_ms * 1e-3) / 1e12, 3),
         "hbm_gbs_algorithmic": round(tot_bytes / (tot_ms * 1e-3) / 1e9, 1),
         "sweep": sweep,
-        "roofline": {"bound": "hbm", "kernel": "moe_gemm_kernel<1> (GEMM1 + SwiGLU)", "achieved": round(achieved, 1),
+        "roofline": {"bound": "hbm", "kernel": roof_kernel, "achieved": round(achieved, 1),
                      "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
-                     "peak_source": peak_src, "traffic": _ncu_traffic()},
+                     "peak_source": peak_src, "traffic": traffic},
         "e2e": {"value": round(sum(e2e_ms.values()) * 1e3 / n_calls, 3), "unit": "us/call",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": 5 * n_calls * args.steps,
+        "gpu_launches": sum(nkern[T] for T in Ts) * args.steps,
         "clocks": clocks,
     }
     if rank == 0 and not args.no_cpu_baseline:
@@ -288,11 +304,11 @@ def bench_ours(args):
         torch.distributed.destroy_process_group()
 
 
-def _ncu_traffic():
+def _ncu_traffic(key):
     p = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(p):
         try:
-            return json.load(open(p)).get("gemm1_dram_bytes_per_launch")
+            return json.load(open(p)).get(key)
         except (OSError, ValueError):
             return None
     return None

@@ -34,6 +34,7 @@ SIGNATURES = {
     "moe_fp8_ds_version": (ctypes.c_char_p, []),
     "moe_fp8_ds_profile_enable": (ctypes.c_int, [ctypes.c_int]),
     "moe_fp8_ds_profile_last": (ctypes.c_int, [ctypes.POINTER(ctypes.c_float), ctypes.c_int]),
+    "moe_fp8_ds_set_fused_decode": (ctypes.c_int, [ctypes.c_int]),
 }
 
 _lib = None

@@ -2,6 +2,7 @@
 // device workspace, TMA tensor maps and the launch sequence
 //   route+plan -> permute -> GEMM1(+SwiGLU+requant) -> GEMM2(+combine) -> finalize
 // on the caller's stream, with no host synchronisation.
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -117,7 +118,21 @@ size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_
   w.tile_sem2 = reinterpret_cast<int32_t*>(take((size_t)kMaxSplitMTiles * kNT2 * 4));
   w.g_part = reinterpret_cast<float*>(take((size_t)kMaxSplitMTiles * kTileM * kGemm1N * 4));
   w.g2_part = reinterpret_cast<float*>(take((size_t)kMaxSplitMTiles * kTileM * kHidden * 4));
+  // fused decode kernel scratch (independent of T)
+  const int grid = device_sm_count();
+  w.dec.grid = grid;
+  w.dec.slots_cap = e_local;
+  w.dec.g1_cnt = reinterpret_cast<int*>(take((size_t)grid * 4));
+  w.dec.ready = reinterpret_cast<int*>(take((size_t)e_local * 4));
+  w.dec.h_cnt = reinterpret_cast<int*>(take((size_t)kNT2 * 4));
+  w.dec.done = reinterpret_cast<int*>(take(4));
+  w.dec.zero = reinterpret_cast<const float*>(take(4));
   if (zero_bytes) *zero_bytes = off;
+  w.dec.g1_part = reinterpret_cast<float*>(take((size_t)grid * 2 * kDecMaxT * 2 * kBlk * 4));
+  w.dec.g2_part = reinterpret_cast<float*>(take((size_t)grid * 2 * kDecMaxT * 2 * kBlk * 4));
+  w.dec.inter = take((size_t)e_local * kDecMaxT * kInterCols);
+  w.dec.inter_scale = reinterpret_cast<float*>(take((size_t)e_local * kInterBlocks * kDecMaxT * 4));
+  w.dec.status = w.status;
   w.token_rows = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
   w.out_rows = reinterpret_cast<float*>(take((size_t)rows * kHidden * 4));
   w.plan = reinterpret_cast<Plan*>(take(sizeof(Plan)));
@@ -176,6 +191,7 @@ int get_workspace(int64_t T, int e_local, bool routing_only, Workspace** out) {
   layout(nw, t_new, e_local, static_cast<uint8_t*>(base), nullptr, routing_only);
   nw.base = base;
   nw.bytes = bytes;
+  nw.zero_bytes = zero_bytes;
   w = nw;
   *out = &w;
   return MOE_OK;
@@ -198,10 +214,24 @@ int check_device() {
 constexpr int kProfKernels = 5;
 bool g_prof_on = false;
 bool g_prof_valid = false;
+int g_prof_n = kProfKernels;  // intervals recorded by the last call (1 for the fused decode kernel)
 cudaEvent_t g_prof_ev[kProfKernels + 1] = {};
 
 inline void prof_mark(int i, cudaStream_t s) {
   if (g_prof_on) cudaEventRecord(g_prof_ev[i], s);
+}
+
+// Calls with 1..kDecMaxT tokens can be served by the fused decode kernel.
+// It is off by default (the five-kernel pipeline measured faster on the
+// decode sweep); MOE_FP8_DS_FUSED_DECODE=1 in the environment or
+// moe_fp8_ds_set_fused_decode(1) turns it on.
+int g_fused_decode = -1;
+bool fused_decode_enabled() {
+  if (g_fused_decode < 0) {
+    const char* v = getenv("MOE_FP8_DS_FUSED_DECODE");
+    g_fused_decode = (v && v[0] == '1') ? 1 : 0;
+  }
+  return g_fused_decode == 1;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -235,6 +265,36 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
   Workspace* ws = nullptr;
   rc = get_workspace(T, static_cast<int>(E_l), route_only, &ws);
   if (rc) return rc;
+
+  if (logits && !route_only && !out_fp32 && T <= kDecMaxT && fused_decode_enabled()) {
+    // one persistent kernel for routing, both GEMMs and the combine
+    CUtensorMap mw1, mw2, mx1, mx2;
+    if (!make_map(&mw1, w1, kHidden, static_cast<uint64_t>(E_l) * kGemm1N) ||
+        !make_map(&mw2, w2, kInter, static_cast<uint64_t>(E_l) * kHidden) ||
+        !make_map(&mx1, hidden, kHidden, static_cast<uint64_t>(T), kDecMaxT) ||
+        !make_map(&mx2, ws->dec.inter, kInterCols, static_cast<uint64_t>(ws->dec.slots_cap) * kDecMaxT, kDecMaxT))
+      return MOE_ERR_CUDA;
+    DecodeCall dc{};
+    dc.logits = logits;
+    dc.bias = static_cast<const uint16_t*>(bias);
+    dc.hidden_scale = hidden_scale;
+    dc.w13_scale = s1;
+    dc.w2_scale = s2;
+    dc.T = static_cast<int>(T);
+    dc.offset = static_cast<int>(offset);
+    dc.e_local = static_cast<int>(E_l);
+    dc.scale = static_cast<float>(scale);
+    dc.out = out;
+    dc.user_ids = user_ids;
+    dc.user_w = user_w;
+    dc.user_counts = user_counts;
+    prof_mark(0, s);
+    if (launch_decode(ws->dec, mw1, mw2, mx1, mx2, dc, s) != cudaSuccess) return MOE_ERR_CUDA;
+    prof_mark(1, s);
+    g_prof_n = 1;
+    g_prof_valid = g_prof_on;
+    return MOE_OK;
+  }
 
   RouteArgs ra{};
   ra.logits = logits;
@@ -279,6 +339,7 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
   prof_mark(4, s);
   if (launch_finalize(*ws, static_cast<int>(T), out, out_fp32, s) != cudaSuccess) return MOE_ERR_CUDA;
   prof_mark(5, s);
+  g_prof_n = kProfKernels;
   g_prof_valid = g_prof_on;
   return MOE_OK;
 }
@@ -356,7 +417,9 @@ int moe_fp8_ds_device_status(void* stream) {
     unsigned v = 0;
     if (cudaMemcpy(&v, kv.second.status, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return MOE_ERR_CUDA;
     if (v) {
-      cudaMemset(kv.second.status, 0, 4);
+      // a kernel gave up part-way: counters and partial sums that are normally
+      // left at zero may not be; clear them (this also clears the status word)
+      cudaMemset(kv.second.base, 0, kv.second.zero_bytes);
       rc = MOE_ERR_DEVICE_TIMEOUT;
     }
   }
@@ -403,12 +466,19 @@ int moe_fp8_ds_profile_last(float* ms_out, int n) {
   std::lock_guard<std::mutex> lk(g_mu);
   if (!ms_out || n <= 0) return -MOE_ERR_INVALID_ARG;
   if (!g_prof_valid) return 0;
-  if (cudaEventSynchronize(g_prof_ev[kProfKernels]) != cudaSuccess) return -MOE_ERR_CUDA;
-  int k = n < kProfKernels ? n : kProfKernels;
+  if (cudaEventSynchronize(g_prof_ev[g_prof_n]) != cudaSuccess) return -MOE_ERR_CUDA;
+  int k = n < g_prof_n ? n : g_prof_n;
   for (int i = 0; i < k; ++i) {
     if (cudaEventElapsedTime(&ms_out[i], g_prof_ev[i], g_prof_ev[i + 1]) != cudaSuccess) return -MOE_ERR_CUDA;
   }
   return k;
+}
+
+int moe_fp8_ds_set_fused_decode(int on) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  const int prev = fused_decode_enabled() ? 1 : 0;
+  if (on >= 0) g_fused_decode = on ? 1 : 0;
+  return prev;
 }
 
 const char* moe_fp8_ds_version(void) { return "moe_fp8_ds 0.1 sm_100a"; }

@@ -65,6 +65,7 @@ struct GemmCfg {
 constexpr int kMaxStages = 5;
 constexpr int kRingBytes = 200 * 1024;          // >= kRing of every configuration
 constexpr int kSkinnyMaxRows = 64;
+constexpr int kDecMaxT = 64;                   // largest call served by the fused decode kernel
 
 constexpr int kGemmThreads = 608;             // 19 warps
 constexpr int kScaleWarp = 2;                 // warp 2 streams block scales into shared memory

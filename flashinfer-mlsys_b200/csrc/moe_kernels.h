@@ -10,6 +10,40 @@
 
 namespace moe {
 
+// ---- fused decode kernel (1 <= T <= kDecMaxT) ----
+// Scratch of the fused decode kernel (device memory; the counters, partial
+// sums and the combine accumulator start at zero and are left at zero).
+struct DecodeBuffers {
+  int grid = 0;                // CTAs of the launch (the device's SM count)
+  int slots_cap = 0;           // touched local experts it can hold
+  uint8_t* inter = nullptr;    // [slots_cap][64][4096] two-term e4m3 intermediate
+  float* inter_scale = nullptr;  // [slots_cap][16][64]
+  float* g1_part = nullptr;    // [grid][2][64][256] pieces of split GEMM1 units
+  float* g2_part = nullptr;    // [grid][2][64][256] pieces of GEMM2 units
+  int* g1_cnt = nullptr;       // [grid]
+  int* ready = nullptr;        // [slots_cap]
+  int* h_cnt = nullptr;        // [28]
+  int* done = nullptr;         // [1]
+  const float* zero = nullptr;  // one 0.0f
+  unsigned* status = nullptr;
+};
+
+struct DecodeCall {
+  const float* logits;
+  const uint16_t* bias;
+  const float* hidden_scale;
+  const float* w13_scale;
+  const float* w2_scale;
+  int T;
+  int offset;
+  int e_local;
+  float scale;
+  void* out;                   // bf16 [T][7168]
+  int32_t* user_ids;
+  float* user_w;
+  int32_t* user_counts;
+};
+
 // Device workspace of one call (all pointers device memory).
 struct Workspace {
   int64_t t_cap = 0;       // tokens (rows of the caller's tensors) it was sized for
@@ -37,8 +71,10 @@ struct Workspace {
   float* out_rows = nullptr;       // [rows_cap][7168] routing-weighted expert output of every permuted row
   int32_t* token_rows = nullptr;   // [t_cap][8] permuted rows of each token, ascending expert id, -1 padded
   unsigned* status = nullptr;      // device status word (kErrTimeout ...)
+  DecodeBuffers dec;               // scratch of the fused decode kernel
   void* base = nullptr;            // single allocation backing everything above
   size_t bytes = 0;
+  size_t zero_bytes = 0;           // length of the prefix that must be zero between calls
 };
 
 struct RouteArgs {
@@ -96,6 +132,14 @@ cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CU
 cudaError_t launch_gemm2(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
                          const float* w_scale, cudaStream_t s, bool skinny);
 cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32, cudaStream_t s);
+
+size_t decode_smem_bytes();
+// map_w13: W13 [E_l*4096][7168] 128-row boxes; map_w2: W2 [E_l*7168][2048]
+// 128-row boxes; map_x1: hidden_states [T][7168] 64-row boxes (rows >= T read
+// as zero); map_x2: DecodeBuffers::inter [slots_cap*64][4096] 64-row boxes.
+cudaError_t launch_decode(const DecodeBuffers& d, const CUtensorMap& map_w13, const CUtensorMap& map_w2,
+                          const CUtensorMap& map_x1, const CUtensorMap& map_x2, const DecodeCall& c,
+                          cudaStream_t s);
 
 
 }  // namespace moe

@@ -10,6 +10,7 @@
 // and the local dispatch of ref_moe.py:131-148 / kernel.cu:201-232
 // (expert id - local_expert_offset in [0, E_local)).
 #include "moe_kernels.h"
+#include "moe_routing.cuh"
 
 namespace moe {
 
@@ -23,21 +24,6 @@ constexpr int kMinTokensPerCta = 8;
 #define MOE_SPLIT_UNIT_OVERHEAD 16
 #endif
 constexpr int kSplitUnitOverhead = MOE_SPLIT_UNIT_OVERHEAD;
-
-// Sort 8 composite keys descending (19-comparator network, all-0/1-input verified).
-__device__ __forceinline__ void cmpswap(uint64_t& a, uint64_t& b) {
-  const uint64_t hi = a > b ? a : b, lo = a > b ? b : a;
-  a = hi;
-  b = lo;
-}
-__device__ __forceinline__ void sort8_desc(uint64_t (&c)[8]) {
-  cmpswap(c[0], c[2]); cmpswap(c[1], c[3]); cmpswap(c[4], c[6]); cmpswap(c[5], c[7]);
-  cmpswap(c[0], c[4]); cmpswap(c[1], c[5]); cmpswap(c[2], c[6]); cmpswap(c[3], c[7]);
-  cmpswap(c[0], c[1]); cmpswap(c[2], c[3]); cmpswap(c[4], c[5]); cmpswap(c[6], c[7]);
-  cmpswap(c[2], c[4]); cmpswap(c[3], c[5]);
-  cmpswap(c[1], c[4]); cmpswap(c[3], c[6]);
-  cmpswap(c[1], c[2]); cmpswap(c[3], c[4]); cmpswap(c[5], c[6]);
-}
 
 // One warp, one token: copy the e4m3 row (7168 B) and its 56 block scales to
 // every local expert slot the token was routed to, and record the token's
@@ -118,84 +104,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
     int my_id = -1;     // lane k < 8 holds the k-th selected expert
     float my_w = 0.f;
     if (a.logits != nullptr) {
-      // ---- lane l owns experts [8l, 8l+8): group g = l / 4 ----
-      const float4* lp = reinterpret_cast<const float4*>(a.logits + (size_t)t * kExperts + lane * 8);
-      float4 x0 = __ldg(lp), x1 = __ldg(lp + 1);
-      float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-      uint4 braw = __ldg(reinterpret_cast<const uint4*>(a.bias + lane * 8));
-      const uint32_t bw[4] = {braw.x, braw.y, braw.z, braw.w};
-      float s[8], sb[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        uint32_t bits = (i & 1) ? (bw[i >> 1] & 0xFFFF0000u) : (bw[i >> 1] << 16);
-        float b = __uint_as_float(bits);
-        s[i] = 1.0f / (1.0f + expf(-x[i]));
-        sb[i] = s[i] + b;
-      }
-      // ---- top-2 of the group (4 lanes) ----
-      float m1 = -INFINITY, m2 = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float v = sb[i];
-        if (v > m1) { m2 = m1; m1 = v; } else if (v > m2) { m2 = v; }
-      }
-#pragma unroll
-      for (int off = 1; off <= 2; off <<= 1) {
-        float o1 = __shfl_xor_sync(0xffffffffu, m1, off);
-        float o2 = __shfl_xor_sync(0xffffffffu, m2, off);
-        float n1 = fmaxf(m1, o1);
-        float n2 = fmaxf(fminf(m1, o1), fmaxf(m2, o2));
-        m1 = n1; m2 = n2;
-      }
-      const float gscore = m1 + m2;
-      const int g = lane >> 2;
-      int rank = 0;
-#pragma unroll
-      for (int gg = 0; gg < kGroups; ++gg) {
-        float o = __shfl_sync(0xffffffffu, gscore, gg * 4);
-        rank += (o > gscore || (o == gscore && gg < g)) ? 1 : 0;
-      }
-      const bool kept = rank < kTopKGroups;
-      // ---- top-8 of the kept candidates, ordered by (sb desc, expert id asc) ----
-      // composite key: order-preserving bits of sb in the high word, 0xFFFF - id
-      // in the low word; 0 marks a candidate of a dropped group.
-      uint64_t c[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint32_t u = __float_as_uint(sb[i]);
-        const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-        c[i] = kept ? ((static_cast<uint64_t>(ord) << 32) | static_cast<uint32_t>(0xFFFF - (lane * 8 + i))) : 0ull;
-      }
-      sort8_desc(c);
-      // 8 rounds: warp max of the lane heads (key word, then id word), the
-      // winning lane pops its head.
-      int sel = 0;
-#pragma unroll 1
-      for (int k = 0; k < kTopK; ++k) {
-        const uint32_t hk = static_cast<uint32_t>(c[0] >> 32);
-        const uint32_t mk = __reduce_max_sync(0xffffffffu, hk);
-        const uint32_t lo = (hk == mk) ? static_cast<uint32_t>(c[0]) : 0u;
-        const uint32_t ml = __reduce_max_sync(0xffffffffu, lo);
-        const bool win = (hk == mk) && (lo == ml);
-        if (lane == k) sel = 0xFFFF - static_cast<int>(ml);
-        if (win) {
-#pragma unroll
-          for (int i = 0; i < 7; ++i) c[i] = c[i + 1];
-          c[7] = 0ull;
-        }
-      }
-      // weight numerators: recompute the un-biased sigmoid of the chosen expert
-      // (same instruction sequence as above, so the value is identical)
-      float sel_s = 0.f;
-      if (lane < kTopK) {
-        const float xl = __ldg(a.logits + (size_t)t * kExperts + sel);
-        sel_s = 1.0f / (1.0f + expf(-xl));
-        my_id = sel;
-      }
-      float ssum = sel_s;
-#pragma unroll
-      for (int off = 4; off >= 1; off >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, off);
-      my_w = (sel_s / (ssum + 1e-20f)) * a.scale;
+      route_token_warp(a.logits + (size_t)t * kExperts, a.bias, a.scale, lane, my_id, my_w);
     } else if (lane < kTopK) {
       my_id = __ldg(a.given_ids + (size_t)t * kTopK + lane);
       my_w = __ldg(a.given_w + (size_t)t * kTopK + lane);

@@ -145,11 +145,23 @@ int moe_fp8_ds_experts(const void* hidden_states, const float* hidden_states_sca
  * around each of its kernels. moe_fp8_ds_profile_last() synchronises on the
  * last call's final event and writes the milliseconds of its kernels
  * (route, permute, gemm1, gemm2, finalize) to ms_out[0..4]; returns the number
- * written, or a negative status. Disabled by default; enabling costs one
- * event record per kernel.
+ * written, or a negative status. A call served by the fused decode kernel
+ * records one interval (that kernel) and returns 1. Disabled by default;
+ * enabling costs one event record per kernel.
  */
 int moe_fp8_ds_profile_enable(int on);
 int moe_fp8_ds_profile_last(float* ms_out, int n);
+
+/*
+ * Selects how moe_fp8_ds_kernel / moe_fp8_ds_kernel_ex serve calls with
+ * 1 <= seq_len <= 64 (no reference counterpart: path selection of this
+ * library). on = 1: one persistent kernel does routing, both GEMMs and the
+ * combine. on = 0 (the default, unless the environment sets
+ * MOE_FP8_DS_FUSED_DECODE=1): the five-kernel pipeline that larger calls use.
+ * on < 0 only queries. Returns the previous setting. Both give results within
+ * the same tolerance of the reference.
+ */
+int moe_fp8_ds_set_fused_decode(int on);
 
 /* Human-readable text for a status code (static storage, never NULL). */
 const char* moe_fp8_ds_status_string(int status);
