@@ -134,7 +134,7 @@ size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_
   w.dec.inter_scale = reinterpret_cast<float*>(take((size_t)e_local * kInterBlocks * kDecMaxT * 4));
   w.dec.status = w.status;
   w.token_rows = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
-  w.out_rows = reinterpret_cast<float*>(take((size_t)rows * kHidden * 4));
+  w.out_rows = reinterpret_cast<__nv_bfloat16*>(take((size_t)rows * kHidden * 2));
   w.plan = reinterpret_cast<Plan*>(take(sizeof(Plan)));
   w.topk_ids = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
   w.topk_w = reinterpret_cast<float*>(take(Tz * kTopK * 4));

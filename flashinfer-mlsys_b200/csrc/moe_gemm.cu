@@ -9,7 +9,8 @@
 //   GEMM2 (kMode = 2): O[r, :] = (hi + lo)[r, :] x W2[e]^T over 16 K blocks:
 //     per block the hi and lo tiles are both multiplied against the same W2
 //     tile into one TMEM partial (they share the scale s), then
-//     out_rows[r, :] = routing_weight(r) * O[r, :]  (ref_moe.py:162-166).
+//     out_rows[r, :] = bf16(routing_weight(r) * O[r, :])  (ref_moe.py:162-166;
+//     the combine sums these rows in fp32).
 //
 // Warp roles (576 threads, one CTA per SM):
 //   warp 0      TMA producer (one elected lane): A tile 128x128 + two B slabs
@@ -44,7 +45,7 @@ struct GemmArgs {
   float* g_part;            // GEMM1 split-K scratch: [kMaxSplitMTiles*128][4096]
   int32_t* tile_sem;        // GEMM1 split-K counters: [kMaxSplitMTiles][16]
   const float* row_weight;  // GEMM2: routing weight of each permuted row
-  float* out_rows;          // GEMM2 out: [rows_cap][7168] weighted expert outputs
+  __nv_bfloat16* out_rows;  // GEMM2 out: [rows_cap][7168] weighted expert outputs (bf16)
   float* g2_part;           // GEMM2 split-K scratch: [kMaxSplitMTiles*128][7168]
   int32_t* tile_sem2;       // GEMM2 split-K counters: [kMaxSplitMTiles][28]
   unsigned* status;
@@ -141,6 +142,19 @@ __device__ __forceinline__ void promote16(float* acc, const float (&v)[16], floa
 // x * sigmoid(x) (ref_moe.py:157) with the fast exponential and reciprocal
 // intrinsics: relative error ~1e-7, far below the e4m3 requantisation that
 // follows, and a short code path (no division slow path).
+// 16 consecutive bf16 values w * v[0..15] (round to nearest even) as two uint4
+__device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, float w, const float* v) {
+  uint32_t u[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    __nv_bfloat162 b = __floats2bfloat162_rn(w * v[2 * i], w * v[2 * i + 1]);
+    u[i] = *reinterpret_cast<uint32_t*>(&b);
+  }
+  uint4* d = reinterpret_cast<uint4*>(dst);
+  d[0] = make_uint4(u[0], u[1], u[2], u[3]);
+  d[1] = make_uint4(u[4], u[5], u[6], u[7]);
+}
+
 __device__ __forceinline__ float silu_ref(float x) { return x * __frcp_rn(1.0f + __expf(-x)); }
 
 __device__ __forceinline__ float e4m3_byte_to_f32(uint32_t b) {
@@ -517,12 +531,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (do_swiglu) swiglu_quant_store(acc, acc + 32, cg, row_in_tile, valid, row, x.n, ctl, p, es);
       } else {
         const float w = valid ? __ldg(p.row_weight + row) : 0.f;
-        float4* dst = reinterpret_cast<float4*>(p.out_rows + row * kHidden + x.n * kTileN + cg * 64);
+        __nv_bfloat16* dst = p.out_rows + row * kHidden + x.n * kTileN + cg * 64;
         if (split == 1) {
           if (valid) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              dst[i] = make_float4(w * acc[4 * i], w * acc[4 * i + 1], w * acc[4 * i + 2], w * acc[4 * i + 3]);
+            for (int i = 0; i < 64; i += 16) store_bf16x16(dst + i, w, acc + i);
           }
         } else {
           // split-K: partial sums meet in fp32 scratch; the last arriving CTA
@@ -545,14 +558,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (valid) {
               // all loads first (independent), then the stores
               float4* pg = reinterpret_cast<float4*>(g);
-              float4 v[16];
-#pragma unroll
-              for (int i = 0; i < 16; ++i) v[i] = __ldcg(pg + i);
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
-                dst[i] = v[i];
-                __stcg(pg + i, make_float4(0.f, 0.f, 0.f, 0.f));
+                const float4 a4 = __ldcg(pg + i);
+                acc[4 * i] = a4.x; acc[4 * i + 1] = a4.y; acc[4 * i + 2] = a4.z; acc[4 * i + 3] = a4.w;
               }
+#pragma unroll
+              for (int i = 0; i < 16; ++i) __stcg(pg + i, make_float4(0.f, 0.f, 0.f, 0.f));
+#pragma unroll
+              for (int i = 0; i < 64; i += 16) store_bf16x16(dst + i, 1.0f, acc + i);
             }
             if (warp == kEpiWarp0 && lane == 0) p.tile_sem2[x.gm * kNT2 + x.n] = 0;
           }

@@ -68,7 +68,7 @@ struct Workspace {
   int32_t* tile_sem = nullptr;     // [kMaxSplitMTiles][16] GEMM1 split-K arrival counters (kept zero)
   float* g2_part = nullptr;        // [kMaxSplitMTiles*128][7168] GEMM2 split-K partial sums (kept zero)
   int32_t* tile_sem2 = nullptr;    // [kMaxSplitMTiles][28] GEMM2 split-K arrival counters (kept zero)
-  float* out_rows = nullptr;       // [rows_cap][7168] routing-weighted expert output of every permuted row
+  __nv_bfloat16* out_rows = nullptr;  // [rows_cap][7168] routing-weighted expert output of every permuted row (bf16)
   int32_t* token_rows = nullptr;   // [t_cap][8] permuted rows of each token, ascending expert id, -1 padded
   unsigned* status = nullptr;      // device status word (kErrTimeout ...)
   DecodeBuffers dec;               // scratch of the fused decode kernel

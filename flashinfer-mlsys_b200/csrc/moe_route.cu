@@ -211,9 +211,9 @@ __global__ void __launch_bounds__(256) permute_kernel(PermuteArgs a, Workspace w
 }
 
 // out[t, :] = sum over the token's local rows (ascending expert id) of the
-// routing-weighted expert outputs, in fp32, then cast once (ref_moe.py:166-167).
-// Eight columns per thread.
-__global__ void __launch_bounds__(256) finalize_kernel(const float* __restrict__ rows_buf,
+// routing-weighted expert outputs (bf16 rows written by GEMM2), in fp32, then
+// cast once (ref_moe.py:166-167). Eight columns per thread.
+__global__ void __launch_bounds__(256) finalize_kernel(const __nv_bfloat16* __restrict__ rows_buf,
                                                        const int32_t* __restrict__ token_rows,
                                                        void* __restrict__ out, int T, int out_fp32) {
   griddep_wait();
@@ -229,10 +229,12 @@ __global__ void __launch_bounds__(256) finalize_kernel(const float* __restrict__
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
       if (r[k] < 0) break;
-      const float4* src = reinterpret_cast<const float4*>(rows_buf + (size_t)r[k] * kHidden) + 2 * c8;
-      const float4 a = __ldcs(src), b = __ldcs(src + 1);
-      s0.x += a.x; s0.y += a.y; s0.z += a.z; s0.w += a.w;
-      s1.x += b.x; s1.y += b.y; s1.z += b.z; s1.w += b.w;
+      // 8 bf16 columns of the row; bf16 -> f32 is exact (upper half of the word)
+      const uint4 q = __ldcs(reinterpret_cast<const uint4*>(rows_buf + (size_t)r[k] * kHidden) + c8);
+      s0.x += __uint_as_float(q.x << 16); s0.y += __uint_as_float(q.x & 0xFFFF0000u);
+      s0.z += __uint_as_float(q.y << 16); s0.w += __uint_as_float(q.y & 0xFFFF0000u);
+      s1.x += __uint_as_float(q.z << 16); s1.y += __uint_as_float(q.z & 0xFFFF0000u);
+      s1.z += __uint_as_float(q.w << 16); s1.w += __uint_as_float(q.w & 0xFFFF0000u);
     }
     if (out_fp32) {
       float4* o = reinterpret_cast<float4*>(out) + 2 * i;
@@ -297,7 +299,7 @@ cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32,
   int64_t blocks = (n8 + 255) / 256;
   if (blocks > 16 * kSMs) blocks = 16 * kSMs;
   return launch_k(finalize_kernel, dim3((unsigned)blocks), dim3(256), 0, s, true,
-                  static_cast<const float*>(ws.out_rows), static_cast<const int32_t*>(ws.token_rows), out, T,
+                  static_cast<const __nv_bfloat16*>(ws.out_rows), static_cast<const int32_t*>(ws.token_rows), out, T,
                   out_fp32);
 }
 
