@@ -119,9 +119,12 @@ inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, siz
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-int route_ctas_for(int T);
+// Routing grid: tokens per routing CTA and the CTA count for T tokens, with up
+// to ctas_per_sm CTAs per SM for large T.
+constexpr int kRouteCtasPerSm = 4;
+int route_ctas_for(int T, int ctas_per_sm = kRouteCtasPerSm);
 int device_sm_count();  // cached per device
-int tokens_per_cta_for(int T);
+int tokens_per_cta_for(int T, int ctas_per_sm = kRouteCtasPerSm);
 
 cudaError_t launch_route(const Workspace& ws, const RouteArgs& a, cudaStream_t s);
 cudaError_t launch_permute(const Workspace& ws, const PermuteArgs& a, cudaStream_t s);

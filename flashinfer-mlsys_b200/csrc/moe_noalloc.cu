@@ -19,7 +19,7 @@ namespace {
 
 // Limits of the allocation-free router.
 constexpr int kNoAllocMaxTokens = 8192;
-constexpr int kNoAllocMaxCtas = 256;  // route_ctas_for(T) <= 149 for any T
+constexpr int kNoAllocMaxCtas = 256;  // route_ctas_for(T, 1) <= 149 for any T
 
 // Scratch layout inside the static array (byte offsets, 256-byte aligned).
 constexpr size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -105,10 +105,10 @@ extern "C" int moe_fp8_ds_route_noalloc(const float* routing_logits, const void*
   ra.offset = static_cast<int>(local_expert_offset);
   ra.e_local = static_cast<int>(num_local_experts);
   ra.scale = static_cast<float>(routed_scaling_factor);
-  ra.tokens_per_cta = tokens_per_cta_for(ra.T);
+  ra.tokens_per_cta = tokens_per_cta_for(ra.T, 1);
   ra.user_ids = topk_ids_out;
   ra.user_w = topk_weights_out;
   ra.user_counts = expert_counts_out;
-  if (route_ctas_for(ra.T) > kNoAllocMaxCtas) return MOE_ERR_INVALID_ARG;
+  if (route_ctas_for(ra.T, 1) > kNoAllocMaxCtas) return MOE_ERR_INVALID_ARG;
   return launch_route(ws, ra, s) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }

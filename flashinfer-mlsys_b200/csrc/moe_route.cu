@@ -269,22 +269,25 @@ int device_sm_count() {
   return cache[dev];
 }
 
-int tokens_per_cta_for(int T) {
+int tokens_per_cta_for(int T, int ctas_per_sm) {
   // one token per warp for small T (a call with T <= 8 is a single CTA and
-  // needs no cross-CTA handshake); at most ~kSMs routing CTAs for large T
-  int per = (T + kSMs - 1) / kSMs;
+  // needs no cross-CTA handshake); at most ~ctas_per_sm * kSMs routing CTAs
+  // for large T (routing a token is a few hundred dependent warp
+  // instructions, so large calls want several resident CTAs per SM)
+  const int ctas = kSMs * (ctas_per_sm > 0 ? ctas_per_sm : 1);
+  int per = (T + ctas - 1) / ctas;
   per = ((per + 7) / 8) * 8;
   return per < kMinTokensPerCta ? kMinTokensPerCta : per;
 }
 
-int route_ctas_for(int T) {
+int route_ctas_for(int T, int ctas_per_sm) {
   if (T <= 0) return 1;
-  const int per = tokens_per_cta_for(T);
+  const int per = tokens_per_cta_for(T, ctas_per_sm);
   return (T + per - 1) / per;
 }
 
 cudaError_t launch_route(const Workspace& ws, const RouteArgs& a, cudaStream_t s) {
-  const int grid = route_ctas_for(a.T);
+  const int grid = (a.T + a.tokens_per_cta - 1) / a.tokens_per_cta;
   return launch_k(route_plan_kernel, dim3(grid), dim3(kRouteThreads), 0, s, false, a, ws);
 }
 
