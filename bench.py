@@ -46,18 +46,55 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms during timing."""
+    """SM clock and clock-event (throttle) reasons sampled during the timed
+    region: NVML reads every ~2 ms from a background thread (read-only
+    queries), so that even a region of a few milliseconds gets samples;
+    nvidia-smi at 200 ms when NVML is unavailable."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, gpu_index: int):
         self.proc = None
+        self.thread = None
         self.gpu = gpu_index
         self.path = os.path.join("/tmp", f"moe_clocks_{os.getpid()}.csv")
+        self.sm, self.smax, self.reasons = [], None, set()
+
+    def _nvml_loop(self, nv, h, bits):
+        import time as _t
+        while not self.stop:
+            try:
+                self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for name, b in bits.items():
+                    if r & b:
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001 - sampling is best effort
+                break
+            _t.sleep(0.002)
 
     def __enter__(self):
+        try:
+            import threading
+
+            import pynvml as nv
+
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.smax = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                    "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                    "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                    "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+            self.stop = False
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h, bits), daemon=True)
+            self.thread.start()
+            return self
+        except Exception:  # noqa: BLE001 - fall back to nvidia-smi
+            self.thread = None
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
@@ -68,6 +105,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self.stop = True
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -77,26 +117,23 @@ class ClockSampler:
             self.f.close()
 
     def summary(self):
-        if self.proc is None or not os.path.exists(self.path):
+        if self.thread is None and self.proc is not None and os.path.exists(self.path):
+            for line in open(self.path):
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    self.sm.append(float(f[1]))
+                    self.smax = float(f[2])
+                except ValueError:
+                    continue
+                for n, v in zip(self.NAMES, f[5:9]):
+                    if v.lower() == "active":
+                        self.reasons.add(n)
+        if not self.sm:
             return None
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                smax = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": self.smax, "reasons": sorted(self.reasons),
+                "samples": len(self.sm), "source": "nvml" if self.thread is not None else "nvidia-smi"}
 
 
 def _dist():
