@@ -33,6 +33,8 @@ WORKLOADS = {
     "large": ((4096, 8192, 16384), "BASELINE configs[3]: large prefill, +2.0 bias on 4 hot local experts"),
     "ep": ((4096,), "BASELINE configs[4]: full 256-expert layer, expert parallel, 4096 tokens per GPU, "
                     "NCCL all-to-all dispatch/combine"),
+    "quant": ((1, 64, 4096, 16384), "upstream step: BF16 -> FP8 1x128 activation quantisation "
+                                    "(moe_fp8_ds_quantize_act), bf16 ~N(0,1) hidden states"),
 }
 L2_FLUSH_BYTES = 256 << 20
 
@@ -612,6 +614,54 @@ def bench_flashinfer(args):
                       "parity_vs_oracle": parity}), flush=True)
 
 
+def bench_quant(args):
+    """The upstream activation quantiser alone: µs per call and achieved GB/s
+    (14,336 B read + 7,392 B written per token) against the measured HBM peak."""
+    import torch
+
+    pkg = importlib.import_module("flashinfer-mlsys_b200")
+    dev = torch.device("cuda", 0)
+    Ts = tuple(int(t) for t in args.T.split(",")) if args.T else WORKLOADS["quant"][0]
+    hbm_peak, _, peak_src = _peaks()
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    g = torch.Generator(device="cpu").manual_seed(0)
+    xs = {T: torch.randn(T, 7168, generator=g).to(torch.bfloat16).to(dev) for T in Ts}
+    outs = {T: (torch.empty((T, 7168), dtype=torch.float8_e4m3fn, device=dev),
+                torch.empty((56, T), dtype=torch.float32, device=dev)) for T in Ts}
+    for _ in range(args.warmup):
+        for T in Ts:
+            pkg.quantize_activations(xs[T], *outs[T])
+    torch.cuda.synchronize()
+    sweep = {}
+    with ClockSampler(0) as clk:
+        for T in Ts:
+            ms = []
+            for _ in range(args.steps):
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                pkg.quantize_activations(xs[T], *outs[T])
+                e1.record()
+                ms.append((e0, e1))
+            torch.cuda.synchronize()
+            t = statistics.mean(a.elapsed_time(b) for a, b in ms)
+            byts = T * (7168 * 2 + 7168 + 56 * 4)
+            sweep[str(T)] = {"us": round(t * 1e3, 2), "gbs": round(byts / (t * 1e-3) / 1e9, 1),
+                             "hbm_frac": round(byts / (t * 1e-3) / 1e9 / hbm_peak, 4)}
+    big = str(max(Ts))
+    line = {"metric": "us/call and GB/s of the BF16 -> FP8 1x128 activation quantiser", "value": sweep[big]["us"],
+            "unit": f"us/call at T={big}", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": False, "dtype": "bf16 -> e4m3", "data": "synthetic ~N(0,1)",
+            "config": {"workload": f"quant: {WORKLOADS['quant'][1]}", "T": list(Ts),
+                       "l2": "256 MB L2 flush before every call, outside the timed events"},
+            "sweep": sweep,
+            "roofline": {"bound": "hbm", "kernel": "quant_rows_kernel", "achieved": sweep[big]["gbs"],
+                         "peak": hbm_peak, "unit": "GB/s", "frac": sweep[big]["hbm_frac"],
+                         "peak_source": peak_src},
+            "gpu_launches": len(Ts) * args.steps, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -633,6 +683,8 @@ def main():
         bench_flashinfer(args)
     elif args.workload == "ep":
         bench_ep(args)
+    elif args.workload == "quant":
+        bench_quant(args)
     else:
         bench_ours(args)
 

@@ -16,11 +16,12 @@ from .binding import (  # noqa: F401
     experts,
     kernel,
     kernel_ex,
+    quantize_activations,
     route,
 )
 from . import workloads  # noqa: F401
 from ._lib import MoeError, lib_path, load  # noqa: F401
 
 __all__ = [
-    "kernel", "kernel_ex", "route", "experts", "device_status", "workloads", "MoeError", "load", "lib_path",
+    "kernel", "kernel_ex", "route", "experts", "quantize_activations", "device_status", "workloads", "MoeError", "load", "lib_path",
 ]

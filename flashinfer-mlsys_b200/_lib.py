@@ -35,6 +35,7 @@ SIGNATURES = {
     "moe_fp8_ds_profile_enable": (ctypes.c_int, [ctypes.c_int]),
     "moe_fp8_ds_profile_last": (ctypes.c_int, [ctypes.POINTER(ctypes.c_float), ctypes.c_int]),
     "moe_fp8_ds_set_fused_decode": (ctypes.c_int, [ctypes.c_int]),
+    "moe_fp8_ds_quantize_act": (ctypes.c_int, [_vp, _c_int64, _vp, _vp, _vp]),
 }
 
 _lib = None

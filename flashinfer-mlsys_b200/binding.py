@@ -227,6 +227,30 @@ def experts(
     _lib.check(rc, "moe_fp8_ds_experts")
 
 
+@torch.no_grad()
+def quantize_activations(hidden_bf16: torch.Tensor, hidden_states: torch.Tensor | None = None,
+                         hidden_states_scale: torch.Tensor | None = None):
+    """BF16 hidden states [seq_len, 7168] -> the layer's FP8 input: e4m3
+    [seq_len, 7168] and transposed f32 scales [56, seq_len], one scale
+    max(amax / 448, 1e-12) per 1x128 block, round to nearest even. Writes the
+    given output tensors (allocated if None) and returns them."""
+    _need(hidden_bf16.dim() == 2, "hidden_bf16 must be 2-D [seq_len, 7168]")
+    T = hidden_bf16.shape[0]
+    _tensor(hidden_bf16, "hidden_bf16", torch.bfloat16, (T, HIDDEN_SIZE))
+    dev = hidden_bf16.device
+    if hidden_states is None:
+        hidden_states = torch.empty((T, HIDDEN_SIZE), dtype=_E4M3, device=dev)
+    if hidden_states_scale is None:
+        hidden_states_scale = torch.empty((HIDDEN_SIZE // BLOCK_Q, T), dtype=torch.float32, device=dev)
+    _tensor(hidden_states, "hidden_states", _E4M3, (T, HIDDEN_SIZE))
+    _tensor(hidden_states_scale, "hidden_states_scale", torch.float32, (HIDDEN_SIZE // BLOCK_Q, T))
+    lib = _lib.load()
+    rc = _call(dev, lib.moe_fp8_ds_quantize_act, hidden_bf16.data_ptr(), T, hidden_states.data_ptr(),
+               hidden_states_scale.data_ptr(), _stream(dev))
+    _lib.check(rc, "moe_fp8_ds_quantize_act")
+    return hidden_states, hidden_states_scale
+
+
 def device_status(stream=None) -> int:
     """Synchronise and return the library's device status (0 = ok)."""
     s = torch.cuda.current_stream().cuda_stream if stream is None else stream

@@ -392,6 +392,22 @@ int moe_fp8_ds_experts(const void* hidden_states, const float* hidden_states_sca
                       output_fp32 ? 1 : 0, num_rows, num_local_experts, nullptr, nullptr, nullptr, stream, false);
 }
 
+int moe_fp8_ds_quantize_act(const void* hidden_bf16, int64_t seq_len, void* hidden_fp8_out, float* hidden_scale_out,
+                            void* stream) {
+  if (seq_len < 0 || seq_len > (int64_t(1) << 24)) return MOE_ERR_INVALID_ARG;
+  if (seq_len == 0) return check_device();  // empty tensors may carry null data pointers
+  if (!hidden_bf16 || !hidden_fp8_out || !hidden_scale_out) return MOE_ERR_INVALID_ARG;
+  if (!aligned16(hidden_bf16) || !aligned16(hidden_fp8_out) ||
+      (reinterpret_cast<uintptr_t>(hidden_scale_out) & 3u))
+    return MOE_ERR_ALIGNMENT;
+  int rc = check_device();
+  if (rc) return rc;
+  if (launch_quant_rows(hidden_bf16, static_cast<int>(seq_len), hidden_fp8_out, hidden_scale_out,
+                        static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  return MOE_OK;
+}
+
 const char* moe_fp8_ds_status_string(int status) {
   switch (status) {
     case MOE_OK: return "ok";

@@ -136,6 +136,9 @@ cudaError_t launch_gemm2(const Workspace& ws, const CUtensorMap& map_a, const CU
                          const float* w_scale, cudaStream_t s, bool skinny);
 cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32, cudaStream_t s);
 
+// BF16 [T][7168] -> e4m3 [T][7168] + f32 scales [56][T] (1x128 blocks, amax / 448)
+cudaError_t launch_quant_rows(const void* x, int T, void* q, float* scale, cudaStream_t s);
+
 size_t decode_smem_bytes();
 // map_w13: W13 [E_l*4096][7168] 128-row boxes; map_w2: W2 [E_l*7168][2048]
 // 128-row boxes; map_x1: hidden_states [T][7168] 64-row boxes (rows >= T read

@@ -163,6 +163,18 @@ int moe_fp8_ds_profile_last(float* ms_out, int n);
  */
 int moe_fp8_ds_set_fused_decode(int on);
 
+/*
+ * The step upstream of the layer (no counterpart in the reference's solution;
+ * its harness supplies pre-quantised inputs, reference moe/ref_moe.json:57-80):
+ * BF16 hidden states [seq_len][7168] -> hidden_fp8_out e4m3 [seq_len][7168]
+ * and hidden_scale_out f32 [56][seq_len] (transposed, the layer's input
+ * format). Per 1x128 block: s = max(amax|x| / 448, 1e-12), q = e4m3(x / s)
+ * with an IEEE division and round-to-nearest-even, the recipe of the layer's
+ * input definition. Asynchronous on `stream`; 16-byte aligned rows.
+ */
+int moe_fp8_ds_quantize_act(const void* hidden_bf16, int64_t seq_len, void* hidden_fp8_out, float* hidden_scale_out,
+                            void* stream);
+
 /* Human-readable text for a status code (static storage, never NULL). */
 const char* moe_fp8_ds_status_string(int status);
 

@@ -183,6 +183,42 @@ def moe_forward(logits, bias, hidden_u8, hidden_scale, get_expert, offset: int, 
 
 
 # ---------------------------------------------------------------------------
+# Upstream step: BF16 activations -> the layer's FP8 input.
+# ---------------------------------------------------------------------------
+_E4M3_POS = E4M3[:0x7F].astype(np.float64)  # codes 0x00..0x7e, ascending finite values 0..448
+
+
+def f32_to_e4m3_rne(y: np.ndarray) -> np.ndarray:
+    """float32 -> e4m3fn byte, round to nearest (ties to the even code),
+    magnitudes above 448 saturating to 448 (the inputs here never exceed 448
+    by more than one rounding of a division). Sign kept, -0.0 -> 0x80."""
+    y = np.asarray(y, dtype=np.float32)
+    a = np.minimum(np.abs(y).astype(np.float64), 448.0)
+    idx = np.clip(np.searchsorted(_E4M3_POS, a, side="left"), 1, 0x7E)
+    lo, hi = _E4M3_POS[idx - 1], _E4M3_POS[idx]
+    d_lo, d_hi = a - lo, hi - a
+    code = np.where(d_lo < d_hi, idx - 1, np.where(d_hi < d_lo, idx, np.where((idx - 1) % 2 == 0, idx - 1, idx)))
+    code = code.astype(np.uint8)
+    return np.where(np.signbit(y), code | np.uint8(0x80), code).astype(np.uint8)
+
+
+def quant_rows_1x128(x: np.ndarray):
+    """[T, 7168] float32 (bf16 values) -> (e4m3 bytes [T, 7168], f32 scales [56, T]).
+
+    The layer's input format (reference moe/ref_moe.json:57-80, hidden_states
+    and the transposed hidden_states_scale): one scale per 1x128 block,
+    s = max(amax|x| / 448, 1e-12), q = e4m3(x / s) with a float32 division;
+    the same amax / 448 recipe the reference uses for its intermediate
+    (solution/triton/dsl-temp1.py:479-481)."""
+    x = np.asarray(x, dtype=np.float32)
+    T = x.shape[0]
+    xb = x.reshape(T, H // BLOCK, BLOCK)
+    s = np.maximum(np.abs(xb).max(axis=-1) / np.float32(448.0), np.float32(1e-12)).astype(np.float32)
+    q = f32_to_e4m3_rne((xb / s[..., None]).astype(np.float32))
+    return q.reshape(T, H), np.ascontiguousarray(s.T)
+
+
+# ---------------------------------------------------------------------------
 # Comparison helpers used by the tests.
 # ---------------------------------------------------------------------------
 def routing_mismatch_is_tie(routing: dict, t: int, ulps: int = 4) -> bool:
