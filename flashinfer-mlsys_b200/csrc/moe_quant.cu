@@ -8,8 +8,14 @@
 // the division, which rounds back to 448). This is the recipe of the layer's
 // input definition (amax / 448 per 1x128 block) and of the intermediate
 // requantisation in reference solution/triton/dsl-temp1.py:479-481. The
-// division is an IEEE division (not a multiply by a reciprocal), so the
-// bytes match a float32 host computation exactly.
+// quotient must be the correctly rounded float32 x / s (e4m3 rounding of a
+// 1-ulp-off quotient can differ), so the bytes match a float32 host
+// computation exactly. It is formed with Markstein's correction (P. Markstein,
+// IA-64 division, 1990): with r = RN(1/s), q0 = RN(x r), e = x - q0 s
+// (exact, one fma) and q = RN(q0 + e r) is the correctly rounded quotient
+// when x and s are normal numbers (s >= 1e-12 here; a quotient small enough
+// for e to underflow rounds to e4m3 zero either way). Two fmas per element
+// instead of an IEEE division.
 //
 // One warp handles one token at a time, two 128-column blocks per step: lanes
 // 0-15 hold block 2c, lanes 16-31 block 2c+1, 8 bf16 (16 bytes) per lane.
@@ -52,11 +58,19 @@ __global__ void __launch_bounds__(kQuantWarps * 32)
 #pragma unroll
       for (int off = 8; off >= 1; off >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, off));
       const float s = fmaxf(__fdiv_rn(__uint_as_float(mb), 448.0f), 1e-12f);
+      const float r = __frcp_rn(s);
+      float y[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float q0 = f[i] * r;
+        const float e = fmaf(-q0, s, f[i]);
+        y[i] = copysignf(fmaf(e, r, q0), q0);  // keeps -0 for x = -0
+      }
       uint32_t w0 = 0, w1 = 0;
 #pragma unroll
       for (int i = 0; i < 4; i += 2) {
-        w0 |= static_cast<uint32_t>(f2_to_e4m3x2(__fdiv_rn(f[i], s), __fdiv_rn(f[i + 1], s))) << (8 * i);
-        w1 |= static_cast<uint32_t>(f2_to_e4m3x2(__fdiv_rn(f[4 + i], s), __fdiv_rn(f[5 + i], s))) << (8 * i);
+        w0 |= static_cast<uint32_t>(f2_to_e4m3x2(y[i], y[i + 1])) << (8 * i);
+        w1 |= static_cast<uint32_t>(f2_to_e4m3x2(y[4 + i], y[5 + i])) << (8 * i);
       }
       __stcs(dst + c * 32 + lane, make_uint2(w0, w1));
       if ((lane & 15) == 0) scale[(size_t)(2 * c + (lane >> 4)) * T + t] = s;
