@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB_NAME = "libmoe_fp8_ds.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
-SOURCES = ["moe_route.cu", "moe_gemm.cu", "moe_decode.cu", "moe_quant.cu", "moe_api.cu", "moe_noalloc.cu"]
+SOURCES = ["moe_route.cu", "moe_gemm.cu", "moe_decode.cu", "moe_quant.cu", "moe_ep.cu", "moe_api.cu", "moe_noalloc.cu"]
 HEADERS = ["moe_common.cuh", "moe_kernels.h", "moe_routing.cuh"]
 
 NVCC_FLAGS = [

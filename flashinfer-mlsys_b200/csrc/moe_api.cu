@@ -408,6 +408,51 @@ int moe_fp8_ds_quantize_act(const void* hidden_bf16, int64_t seq_len, void* hidd
   return MOE_OK;
 }
 
+int moe_fp8_ds_ep_pack(const void* hidden_states, const float* hidden_states_scale, const int32_t* topk_ids,
+                       const float* topk_weights, int64_t seq_len, const int64_t* send_idx, int64_t num_send,
+                       void* send_buf, void* stream) {
+  if (seq_len < 0 || num_send < 0 || seq_len > (int64_t(1) << 24) || num_send > (int64_t(1) << 27))
+    return MOE_ERR_INVALID_ARG;
+  if (num_send == 0) return check_device();
+  if (!hidden_states || !hidden_states_scale || !topk_ids || !topk_weights || !send_idx || !send_buf)
+    return MOE_ERR_INVALID_ARG;
+  if (!aligned16(hidden_states) || !aligned16(send_buf)) return MOE_ERR_ALIGNMENT;
+  int rc = check_device();
+  if (rc) return rc;
+  if (launch_ep_pack(hidden_states, hidden_states_scale, topk_ids, topk_weights, static_cast<int>(seq_len), send_idx,
+                     static_cast<int>(num_send), send_buf, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  return MOE_OK;
+}
+
+int moe_fp8_ds_ep_unpack(const void* recv_buf, int64_t num_rows, void* hidden_states, float* hidden_states_scale,
+                         int32_t* topk_ids, float* topk_weights, void* stream) {
+  if (num_rows < 0 || num_rows > (int64_t(1) << 27)) return MOE_ERR_INVALID_ARG;
+  if (num_rows == 0) return check_device();
+  if (!recv_buf || !hidden_states || !hidden_states_scale || !topk_ids || !topk_weights) return MOE_ERR_INVALID_ARG;
+  if (!aligned16(recv_buf) || !aligned16(hidden_states)) return MOE_ERR_ALIGNMENT;
+  int rc = check_device();
+  if (rc) return rc;
+  if (launch_ep_unpack(recv_buf, static_cast<int>(num_rows), hidden_states, hidden_states_scale, topk_ids,
+                       topk_weights, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  return MOE_OK;
+}
+
+int moe_fp8_ds_ep_combine(const void* partials, const int32_t* row_of, int64_t seq_len, int64_t world, void* output,
+                          void* stream) {
+  if (seq_len < 0 || seq_len > (int64_t(1) << 24) || world < 1 || world > 64) return MOE_ERR_INVALID_ARG;
+  if (seq_len == 0) return check_device();
+  if (!row_of || !output) return MOE_ERR_INVALID_ARG;
+  if ((partials && !aligned16(partials)) || !aligned16(output)) return MOE_ERR_ALIGNMENT;
+  int rc = check_device();
+  if (rc) return rc;
+  if (launch_ep_combine(partials, row_of, static_cast<int>(seq_len), static_cast<int>(world), output,
+                        static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  return MOE_OK;
+}
+
 const char* moe_fp8_ds_status_string(int status) {
   switch (status) {
     case MOE_OK: return "ok";

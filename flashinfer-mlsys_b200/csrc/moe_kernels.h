@@ -136,6 +136,13 @@ cudaError_t launch_gemm2(const Workspace& ws, const CUtensorMap& map_a, const CU
                          const float* w_scale, cudaStream_t s, bool skinny);
 cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32, cudaStream_t s);
 
+// Expert-parallel token exchange (packed 7456-byte rows, see moe_ep.cu)
+cudaError_t launch_ep_pack(const void* hidden, const float* hidden_scale, const int32_t* ids, const float* w, int T,
+                           const int64_t* idx, int S, void* out, cudaStream_t s);
+cudaError_t launch_ep_unpack(const void* in, int R, void* hidden, float* hidden_scale, int32_t* ids, float* w,
+                             cudaStream_t s);
+cudaError_t launch_ep_combine(const void* back, const int32_t* row_of, int T, int world, void* out, cudaStream_t s);
+
 // BF16 [T][7168] -> e4m3 [T][7168] + f32 scales [56][T] (1x128 blocks, amax / 448)
 cudaError_t launch_quant_rows(const void* x, int T, void* q, float* scale, cudaStream_t s);
 

@@ -18,7 +18,10 @@ call:
 
 The route and expert functions are parameters, so the same bookkeeping runs
 with the CUDA library on GPUs (NCCL) and with CPU functions under a gloo
-process group in the tests.
+process group in the tests. On CUDA tensors the row packing, unpacking and
+the combine are the library's kernels (moe_fp8_ds_ep_pack / _unpack /
+_combine); the torch expressions below are their CPU restatement for the
+gloo tests.
 """
 from __future__ import annotations
 
@@ -35,12 +38,26 @@ E_GLOBAL = 256
 ROW_BYTES = H + HB * 4 + TOPK * 4 + TOPK * 4  # 7456
 
 
+def _lib_call(name, dev, *args):
+    from . import _lib
+    from .binding import _call, _stream
+
+    rc = _call(dev, getattr(_lib.load(), name), *args, _stream(dev))
+    _lib.check(rc, name)
+
+
 def pack_rows(hidden: torch.Tensor, hidden_scale: torch.Tensor, ids: torch.Tensor, w: torch.Tensor,
               idx: torch.Tensor) -> torch.Tensor:
     """Rows ``idx`` of (hidden e4m3 [T,7168], scale f32 [56,T], ids int32 [T,8],
     weights f32 [T,8]) -> uint8 [len(idx), 7456]."""
     n = idx.numel()
     buf = torch.empty((n, ROW_BYTES), dtype=torch.uint8, device=hidden.device)
+    if hidden.is_cuda:
+        idx64 = idx.to(torch.int64).contiguous()
+        _lib_call("moe_fp8_ds_ep_pack", hidden.device, hidden.data_ptr(), hidden_scale.data_ptr(),
+                  ids.contiguous().data_ptr(), w.contiguous().data_ptr(), hidden.shape[0], idx64.data_ptr(), n,
+                  buf.data_ptr())
+        return buf
     buf[:, :H] = hidden.view(torch.uint8).index_select(0, idx)
     buf[:, H:H + HB * 4] = hidden_scale.t().index_select(0, idx).contiguous().view(torch.uint8)
     o = H + HB * 4
@@ -52,6 +69,15 @@ def pack_rows(hidden: torch.Tensor, hidden_scale: torch.Tensor, ids: torch.Tenso
 def unpack_rows(buf: torch.Tensor):
     """uint8 [R, 7456] -> (hidden e4m3 [R,7168], scale f32 [56,R], ids int32 [R,8], weights f32 [R,8])."""
     R = buf.shape[0]
+    if buf.is_cuda:
+        dev = buf.device
+        hidden = torch.empty((R, H), dtype=torch.float8_e4m3fn, device=dev)
+        scale = torch.empty((HB, R), dtype=torch.float32, device=dev)
+        ids = torch.empty((R, TOPK), dtype=torch.int32, device=dev)
+        w = torch.empty((R, TOPK), dtype=torch.float32, device=dev)
+        _lib_call("moe_fp8_ds_ep_unpack", dev, buf.data_ptr(), R, hidden.data_ptr(), scale.data_ptr(),
+                  ids.data_ptr(), w.data_ptr())
+        return hidden, scale, ids, w
     hidden = buf[:, :H].contiguous().view(torch.float8_e4m3fn)
     scale = buf[:, H:H + HB * 4].contiguous().view(torch.float32).reshape(R, HB).t().contiguous()
     o = H + HB * 4
@@ -69,17 +95,27 @@ class Plan:
 
 def dispatch_plan(ids: torch.Tensor, world: int, group=None) -> Plan:
     """Which tokens go to which rank (once per rank, ascending token order),
-    and the exchange of the per-rank row counts."""
+    and the exchange of the per-rank row counts. One host synchronisation:
+    NCCL's all-to-all-v takes its split sizes on the host."""
     e_local = E_GLOBAL // world
     T = ids.shape[0]
-    dest = torch.zeros((T, world), dtype=torch.bool, device=ids.device)
+    dest = torch.zeros((world, T), dtype=torch.bool, device=ids.device)
     owner = (ids.long() // e_local).clamp_(0, world - 1)
-    dest.scatter_(1, owner, True)
-    send_idx = torch.cat([torch.nonzero(dest[:, r], as_tuple=False).flatten() for r in range(world)])
-    send_counts_t = dest.sum(dim=0).to(torch.int64)
+    dest.scatter_(0, owner.t().contiguous(), True)
+    # rank-major flat order: tokens grouped by destination rank, ascending
+    # within a rank; positions from a running count (no size-dependent op, so
+    # no host synchronisation before the count exchange)
+    flat = dest.reshape(-1)
+    n = flat.numel()
+    pos = torch.where(flat, torch.cumsum(flat, 0) - 1, torch.full_like(flat, n, dtype=torch.int64))
+    order = torch.empty(n + 1, dtype=torch.int64, device=ids.device)
+    order.scatter_(0, pos, torch.arange(n, device=ids.device) % T)
+    send_counts_t = dest.sum(dim=1).to(torch.int64)
     recv_counts_t = torch.empty_like(send_counts_t)
     dist.all_to_all_single(recv_counts_t, send_counts_t, group=group)
-    return Plan(send_idx, send_counts_t.tolist(), recv_counts_t.tolist())
+    both = torch.cat([send_counts_t, recv_counts_t]).tolist()
+    send_counts, recv_counts = both[:world], both[world:]
+    return Plan(order[:sum(send_counts)], send_counts, recv_counts)
 
 
 def ep_forward(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden: torch.Tensor,
@@ -112,9 +148,26 @@ def ep_forward(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden:
     back = torch.empty((plan.send_idx.numel(), H), dtype=combine_dtype, device=hidden.device)
     dist.all_to_all_single(back, out_r, output_split_sizes=plan.send_counts,
                            input_split_sizes=plan.recv_counts, group=group)
-    out = torch.zeros((T, H), dtype=torch.float32, device=hidden.device)
-    # rows come back grouped by source rank in rank order; adding rank by rank
-    # sums a token's partials in ascending expert-id order
+    return combine_rows(back, plan, T, world)
+
+
+def combine_rows(back: torch.Tensor, plan: Plan, T: int, world: int) -> torch.Tensor:
+    """Sum each token's returned partial rows in fp32 in rank order (= ascending
+    expert-id order) and cast once to bf16. Rows come back grouped by rank, in
+    the order they were sent."""
+    if back.is_cuda and back.dtype == torch.bfloat16:
+        dev = back.device
+        # row_of[t][q]: the row of token t in the block returned by rank q, -1 if none
+        row_of = torch.full((T, world), -1, dtype=torch.int32, device=dev)
+        if plan.send_idx.numel():
+            q = torch.repeat_interleave(torch.arange(world, device=dev),
+                                        torch.tensor(plan.send_counts, device=dev))
+            row_of[plan.send_idx, q] = torch.arange(plan.send_idx.numel(), dtype=torch.int32, device=dev)
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        _lib_call("moe_fp8_ds_ep_combine", dev, back.data_ptr() if back.numel() else None, row_of.data_ptr(), T,
+                  world, out.data_ptr())
+        return out
+    out = torch.zeros((T, H), dtype=torch.float32, device=back.device)
     off = 0
     for r in range(world):
         n = plan.send_counts[r]

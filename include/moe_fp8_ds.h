@@ -175,6 +175,30 @@ int moe_fp8_ds_set_fused_decode(int on);
 int moe_fp8_ds_quantize_act(const void* hidden_bf16, int64_t seq_len, void* hidden_fp8_out, float* hidden_scale_out,
                             void* stream);
 
+/*
+ * Expert parallelism: the token exchange around moe_fp8_ds_experts when the
+ * 256 experts are sharded over GPUs (no counterpart in the reference, which
+ * runs one rank; the collectives are the caller's NCCL all-to-alls). A packed
+ * row is 7456 bytes: the e4m3 hidden row (7168), its 56 f32 block scales, its
+ * 8 int32 global expert ids and 8 f32 routing weights.
+ *
+ * moe_fp8_ds_ep_pack: send_buf[i] = packed row of token send_idx[i]
+ *   (int64 [num_send]); hidden/scale/ids/weights as for the layer, seq_len rows.
+ * moe_fp8_ds_ep_unpack: splits num_rows packed rows into hidden e4m3
+ *   [num_rows][7168], hidden_scale f32 [56][num_rows], ids int32 [num_rows][8],
+ *   weights f32 [num_rows][8].
+ * moe_fp8_ds_ep_combine: output bf16 [seq_len][7168], output[t] = sum over
+ *   q = 0..world-1 of partials[row_of[t][q]] (bf16 rows, -1 = none) in fp32 in
+ *   rank order, cast once.
+ */
+int moe_fp8_ds_ep_pack(const void* hidden_states, const float* hidden_states_scale, const int32_t* topk_ids,
+                       const float* topk_weights, int64_t seq_len, const int64_t* send_idx, int64_t num_send,
+                       void* send_buf, void* stream);
+int moe_fp8_ds_ep_unpack(const void* recv_buf, int64_t num_rows, void* hidden_states, float* hidden_states_scale,
+                         int32_t* topk_ids, float* topk_weights, void* stream);
+int moe_fp8_ds_ep_combine(const void* partials, const int32_t* row_of, int64_t seq_len, int64_t world, void* output,
+                          void* stream);
+
 /* Human-readable text for a status code (static storage, never NULL). */
 const char* moe_fp8_ds_status_string(int status);
 
