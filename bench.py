@@ -35,6 +35,9 @@ WORKLOADS = {
                     "NCCL all-to-all dispatch/combine"),
     "quant": ((1, 64, 4096, 16384), "upstream step: BF16 -> FP8 1x128 activation quantisation "
                                     "(moe_fp8_ds_quantize_act), bf16 ~N(0,1) hidden states"),
+    "addnorm": ((1, 64, 4096, 16384), "downstream step: residual add + DeepSeek-V3 RMSNorm + FP8 1x128 "
+                                      "quantisation of the layer output (moe_fp8_ds_add_norm_quant), bf16 "
+                                      "~N(0,1) output and residual, eps 1e-6"),
 }
 L2_FLUSH_BYTES = 256 << 20
 
@@ -615,22 +618,37 @@ def bench_flashinfer(args):
 
 
 def bench_quant(args):
-    """The upstream activation quantiser alone: µs per call and achieved GB/s
-    (14,336 B read + 7,392 B written per token) against the measured HBM peak."""
+    """The steps either side of the layer alone, µs per call and achieved GB/s
+    against the measured HBM peak:
+    - quant: the upstream activation quantiser, 14,336 B read + 7,392 B
+      written per token;
+    - addnorm: residual add + RMSNorm + quantisation of the layer output,
+      28,672 B read (output, residual) + 21,728 B written (residual, e4m3,
+      scales) per token."""
     import torch
 
     pkg = importlib.import_module("flashinfer-mlsys_b200")
     dev = torch.device("cuda", 0)
-    Ts = tuple(int(t) for t in args.T.split(",")) if args.T else WORKLOADS["quant"][0]
+    addnorm = args.workload == "addnorm"
+    Ts = tuple(int(t) for t in args.T.split(",")) if args.T else WORKLOADS[args.workload][0]
     hbm_peak, _, peak_src = _peaks()
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     g = torch.Generator(device="cpu").manual_seed(0)
     xs = {T: torch.randn(T, 7168, generator=g).to(torch.bfloat16).to(dev) for T in Ts}
+    res = {T: torch.randn(T, 7168, generator=g).to(torch.bfloat16).to(dev) for T in Ts} if addnorm else {}
+    norm_w = (1.0 + 0.1 * torch.randn(7168, generator=g)).to(torch.bfloat16).to(dev)
     outs = {T: (torch.empty((T, 7168), dtype=torch.float8_e4m3fn, device=dev),
                 torch.empty((56, T), dtype=torch.float32, device=dev)) for T in Ts}
+
+    def call(T):
+        if addnorm:
+            pkg.add_rmsnorm_quantize(xs[T], res[T], norm_w, 1e-6, *outs[T])
+        else:
+            pkg.quantize_activations(xs[T], *outs[T])
+
     for _ in range(args.warmup):
         for T in Ts:
-            pkg.quantize_activations(xs[T], *outs[T])
+            call(T)
     torch.cuda.synchronize()
     sweep = {}
     with ClockSampler(0) as clk:
@@ -640,22 +658,25 @@ def bench_quant(args):
                 flush.zero_()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
-                pkg.quantize_activations(xs[T], *outs[T])
+                call(T)
                 e1.record()
                 ms.append((e0, e1))
             torch.cuda.synchronize()
             t = statistics.mean(a.elapsed_time(b) for a, b in ms)
-            byts = T * (7168 * 2 + 7168 + 56 * 4)
+            byts = T * ((7168 * 4 + 7168 * 2 + 7168 + 56 * 4) if addnorm else (7168 * 2 + 7168 + 56 * 4))
             sweep[str(T)] = {"us": round(t * 1e3, 2), "gbs": round(byts / (t * 1e-3) / 1e9, 1),
                              "hbm_frac": round(byts / (t * 1e-3) / 1e9 / hbm_peak, 4)}
     big = str(max(Ts))
-    line = {"metric": "us/call and GB/s of the BF16 -> FP8 1x128 activation quantiser", "value": sweep[big]["us"],
+    what = ("residual add + RMSNorm + FP8 1x128 quantisation of the layer output" if addnorm
+            else "BF16 -> FP8 1x128 activation quantiser")
+    line = {"metric": f"us/call and GB/s of the {what}", "value": sweep[big]["us"],
             "unit": f"us/call at T={big}", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": False, "dtype": "bf16 -> e4m3", "data": "synthetic ~N(0,1)",
-            "config": {"workload": f"quant: {WORKLOADS['quant'][1]}", "T": list(Ts),
+            "config": {"workload": f"{args.workload}: {WORKLOADS[args.workload][1]}", "T": list(Ts),
                        "l2": "256 MB L2 flush before every call, outside the timed events"},
             "sweep": sweep,
-            "roofline": {"bound": "hbm", "kernel": "quant_rows_kernel", "achieved": sweep[big]["gbs"],
+            "roofline": {"bound": "hbm", "kernel": "add_norm_quant_kernel" if addnorm else "quant_rows_kernel",
+                         "achieved": sweep[big]["gbs"],
                          "peak": hbm_peak, "unit": "GB/s", "frac": sweep[big]["hbm_frac"],
                          "peak_source": peak_src},
             "gpu_launches": len(Ts) * args.steps, "clocks": clk.summary()}
@@ -683,7 +704,7 @@ def main():
         bench_flashinfer(args)
     elif args.workload == "ep":
         bench_ep(args)
-    elif args.workload == "quant":
+    elif args.workload in ("quant", "addnorm"):
         bench_quant(args)
     else:
         bench_ours(args)

@@ -17,11 +17,12 @@ from .binding import (  # noqa: F401
     kernel,
     kernel_ex,
     quantize_activations,
+    add_rmsnorm_quantize,
     route,
 )
 from . import workloads  # noqa: F401
 from ._lib import MoeError, lib_path, load  # noqa: F401
 
 __all__ = [
-    "kernel", "kernel_ex", "route", "experts", "quantize_activations", "device_status", "workloads", "MoeError", "load", "lib_path",
+    "kernel", "kernel_ex", "route", "experts", "quantize_activations", "add_rmsnorm_quantize", "device_status", "workloads", "MoeError", "load", "lib_path",
 ]

@@ -251,6 +251,42 @@ def quantize_activations(hidden_bf16: torch.Tensor, hidden_states: torch.Tensor 
     return hidden_states, hidden_states_scale
 
 
+@torch.no_grad()
+def add_rmsnorm_quantize(x: torch.Tensor, residual: torch.Tensor | None = None,
+                         norm_weight: torch.Tensor | None = None, eps: float = 1e-6,
+                         out: torch.Tensor | None = None, out_scale: torch.Tensor | None = None):
+    """The step after the layer: h = bf16(residual + x) (written back into
+    ``residual``), y = DeepSeek-V3 RMSNorm of h with ``norm_weight`` and
+    ``eps``, then the 1x128 FP8 quantisation of y (the next layer's input
+    format, as ``quantize_activations``). ``residual`` None: h = x;
+    ``norm_weight`` None: y = h. Returns (e4m3 [seq_len, 7168], f32 scales
+    [56, seq_len])."""
+    _need(x.dim() == 2, "x must be 2-D [seq_len, 7168]")
+    T = x.shape[0]
+    _tensor(x, "x", torch.bfloat16, (T, HIDDEN_SIZE))
+    dev = x.device
+    if residual is not None:
+        _tensor(residual, "residual", torch.bfloat16, (T, HIDDEN_SIZE))
+        _need(residual.device == dev, "residual must be on the same device as x")
+    if norm_weight is not None:
+        _tensor(norm_weight, "norm_weight", torch.bfloat16, (HIDDEN_SIZE,))
+        _need(norm_weight.device == dev, "norm_weight must be on the same device as x")
+    _need(float(eps) >= 0.0, "eps must be >= 0")
+    if out is None:
+        out = torch.empty((T, HIDDEN_SIZE), dtype=_E4M3, device=dev)
+    if out_scale is None:
+        out_scale = torch.empty((HIDDEN_SIZE // BLOCK_Q, T), dtype=torch.float32, device=dev)
+    _tensor(out, "out", _E4M3, (T, HIDDEN_SIZE))
+    _tensor(out_scale, "out_scale", torch.float32, (HIDDEN_SIZE // BLOCK_Q, T))
+    lib = _lib.load()
+    rc = _call(dev, lib.moe_fp8_ds_add_norm_quant, x.data_ptr(),
+               None if residual is None else residual.data_ptr(),
+               None if norm_weight is None else norm_weight.data_ptr(), float(eps), T, out.data_ptr(),
+               out_scale.data_ptr(), _stream(dev))
+    _lib.check(rc, "moe_fp8_ds_add_norm_quant")
+    return out, out_scale
+
+
 def device_status(stream=None) -> int:
     """Synchronise and return the library's device status (0 = ok)."""
     s = torch.cuda.current_stream().cuda_stream if stream is None else stream

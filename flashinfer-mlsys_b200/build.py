@@ -16,6 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB_NAME = "libmoe_fp8_ds.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
+INCLUDE = os.path.join(os.path.dirname(HERE), "include")  # moe_fp8_ds.h, the C ABI
 SOURCES = ["moe_route.cu", "moe_gemm.cu", "moe_decode.cu", "moe_quant.cu", "moe_ep.cu", "moe_api.cu", "moe_noalloc.cu"]
 HEADERS = ["moe_common.cuh", "moe_kernels.h", "moe_routing.cuh"]
 
@@ -23,6 +24,7 @@ NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
     "-Xcompiler", "-fPIC",
+    "-I", INCLUDE,
     "-Xptxas", "-v",
 ]
 
@@ -35,7 +37,7 @@ def _nvcc() -> str:
 
 
 def _inputs() -> list[str]:
-    inc = os.path.join(os.path.dirname(HERE), "include", "moe_fp8_ds.h")
+    inc = os.path.join(INCLUDE, "moe_fp8_ds.h")
     return [os.path.join(CSRC, f) for f in SOURCES + HEADERS] + [inc]
 
 

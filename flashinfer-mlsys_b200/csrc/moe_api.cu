@@ -6,7 +6,7 @@
 #include <mutex>
 #include <unordered_map>
 
-#include "../../include/moe_fp8_ds.h"
+#include "moe_fp8_ds.h"
 #include "moe_kernels.h"
 
 using namespace moe;
@@ -404,6 +404,22 @@ int moe_fp8_ds_quantize_act(const void* hidden_bf16, int64_t seq_len, void* hidd
   if (rc) return rc;
   if (launch_quant_rows(hidden_bf16, static_cast<int>(seq_len), hidden_fp8_out, hidden_scale_out,
                         static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  return MOE_OK;
+}
+
+int moe_fp8_ds_add_norm_quant(const void* x_bf16, void* residual_bf16, const void* norm_weight_bf16, float eps,
+                              int64_t seq_len, void* out_fp8, float* out_scale, void* stream) {
+  if (seq_len < 0 || seq_len > (int64_t(1) << 24) || !(eps >= 0.f)) return MOE_ERR_INVALID_ARG;
+  if (seq_len == 0) return check_device();
+  if (!x_bf16 || !out_fp8 || !out_scale) return MOE_ERR_INVALID_ARG;
+  if (!aligned16(x_bf16) || !aligned16(out_fp8) || (residual_bf16 && !aligned16(residual_bf16)) ||
+      (norm_weight_bf16 && !aligned16(norm_weight_bf16)) || (reinterpret_cast<uintptr_t>(out_scale) & 3u))
+    return MOE_ERR_ALIGNMENT;
+  int rc = check_device();
+  if (rc) return rc;
+  if (launch_add_norm_quant(x_bf16, residual_bf16, norm_weight_bf16, eps, static_cast<int>(seq_len), out_fp8,
+                            out_scale, static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return MOE_ERR_CUDA;
   return MOE_OK;
 }

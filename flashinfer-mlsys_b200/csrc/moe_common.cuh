@@ -7,6 +7,11 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+// The kernels use tcgen05, TMEM and TMA: device code exists for sm_100a only.
+#if defined(__CUDA_ARCH__) && !defined(__CUDA_ARCH_FEAT_SM100_ALL)
+#error "build for sm_100a only: nvcc -gencode arch=compute_100a,code=sm_100a"
+#endif
+
 namespace moe {
 
 // ---------------------------------------------------------------------------

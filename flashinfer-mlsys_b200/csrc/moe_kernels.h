@@ -145,6 +145,8 @@ cudaError_t launch_ep_combine(const void* back, const int32_t* row_of, int T, in
 
 // BF16 [T][7168] -> e4m3 [T][7168] + f32 scales [56][T] (1x128 blocks, amax / 448)
 cudaError_t launch_quant_rows(const void* x, int T, void* q, float* scale, cudaStream_t s);
+cudaError_t launch_add_norm_quant(const void* x, void* residual, const void* w, float eps, int T, void* q,
+                                  float* scale, cudaStream_t s);
 
 size_t decode_smem_bytes();
 // map_w13: W13 [E_l*4096][7168] 128-row boxes; map_w2: W2 [E_l*7168][2048]

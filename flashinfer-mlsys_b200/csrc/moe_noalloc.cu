@@ -10,7 +10,7 @@
 // that loads the library until the process exits), so a call never allocates.
 #include <mutex>
 
-#include "../../include/moe_fp8_ds.h"
+#include "moe_fp8_ds.h"
 #include "moe_kernels.h"
 
 using namespace moe;

@@ -176,6 +176,22 @@ int moe_fp8_ds_quantize_act(const void* hidden_bf16, int64_t seq_len, void* hidd
                             void* stream);
 
 /*
+ * The step downstream of the layer (no counterpart in the reference, whose
+ * operator ends at the bf16 output, solution/cuda/kernel.cu:288-291): the
+ * decoder's residual add, the next layer's input RMSNorm and its FP8 1x128
+ * quantisation in one pass over the layer's output `x_bf16` [seq_len][7168].
+ *   h = bf16(residual + x)                  written back to residual_bf16
+ *   y = bf16(w * bf16(h / sqrt(mean(h^2) + eps)))   (DeepSeek-V3 RMSNorm)
+ *   out_fp8, out_scale = the quantisation of moe_fp8_ds_quantize_act of y
+ * residual_bf16 == NULL: h = x (nothing is written back). norm_weight_bf16
+ * [7168] == NULL: y = h (no normalisation). The float32 sum of squares and
+ * every rounding follow a fixed order, so the result is deterministic.
+ * Asynchronous on `stream`; 16-byte aligned rows; eps >= 0.
+ */
+int moe_fp8_ds_add_norm_quant(const void* x_bf16, void* residual_bf16, const void* norm_weight_bf16, float eps,
+                              int64_t seq_len, void* out_fp8, float* out_scale, void* stream);
+
+/*
  * Expert parallelism: the token exchange around moe_fp8_ds_experts when the
  * 256 experts are sharded over GPUs (no counterpart in the reference, which
  * runs one rank; the collectives are the caller's NCCL all-to-alls). A packed

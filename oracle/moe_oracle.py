@@ -218,6 +218,54 @@ def quant_rows_1x128(x: np.ndarray):
     return q.reshape(T, H), np.ascontiguousarray(s.T)
 
 
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """float32 -> nearest-even bfloat16 value, returned as float32."""
+    return bf16_bits_to_f32(f32_to_bf16_bits(np.asarray(x, dtype=np.float32)))
+
+
+def add_rmsnorm_quant(x, residual=None, weight=None, eps: float = 1e-6):
+    """The step after the layer, as the CUDA kernel defines it (no counterpart
+    in the reference, whose operator ends at the bf16 output, solution/cuda/
+    kernel.cu:288-291). x, residual: [T, 7168] float32 holding bf16 values;
+    weight: [7168] bf16 values or None; eps is taken as float32.
+
+      h = bf16(residual + x)        (h = x without a residual)
+      y = bf16(w * bf16(h * r)),  r = 1 / sqrt(sum(h^2) / 7168 + eps)
+      (y = h without a weight), then quant_rows_1x128(y).
+
+    The DeepSeek-V3 decoder's residual add and input RMSNorm (HF transformers
+    DeepseekV3RMSNorm: float32 variance, rsqrt, cast to bf16, times the bf16
+    weight). The float32 sum of squares follows the kernel's order: thread i
+    of 128 owns 8-column chunks c = 128 j + i (j = 0..6) and sums its 56
+    squares in column order; a warp reduces by xor-butterfly (offsets 16, 8,
+    4, 2, 1); the 4 warp sums add as ((w0 + w1) + w2) + w3. r is
+    RN(1 / RN(sqrt(RN(RN(ss / 7168) + eps)))).
+    Returns (h, q bytes [T, 7168], scales [56, T])."""
+    f32 = np.float32
+    x = np.asarray(x, dtype=f32)
+    T = x.shape[0]
+    h = bf16_round(np.asarray(residual, dtype=f32) + x) if residual is not None else x.copy()
+    if weight is None:
+        y = h
+    else:
+        sq = (h * h).astype(f32)                                   # exact for bf16 values
+        per_thread = sq.reshape(T, 7, 128, 8).transpose(0, 2, 1, 3).reshape(T, 128, 56)
+        acc = np.zeros((T, 128), dtype=f32)
+        for i in range(56):
+            acc = (acc + per_thread[:, :, i]).astype(f32)
+        v = acc.reshape(T, 4, 32)
+        lanes = np.arange(32)
+        for off in (16, 8, 4, 2, 1):
+            v = (v + v[:, :, lanes ^ off]).astype(f32)
+        tot = (((v[:, 0, 0] + v[:, 1, 0]).astype(f32) + v[:, 2, 0]).astype(f32) + v[:, 3, 0]).astype(f32)
+        mean = (tot / f32(H)).astype(f32)
+        r = (f32(1.0) / np.sqrt((mean + f32(eps)).astype(f32))).astype(f32)
+        n = bf16_round(h * r[:, None])
+        y = bf16_round(np.asarray(weight, dtype=f32)[None, :] * n)
+    q, sc = quant_rows_1x128(y)
+    return h, q, sc
+
+
 # ---------------------------------------------------------------------------
 # Comparison helpers used by the tests.
 # ---------------------------------------------------------------------------
