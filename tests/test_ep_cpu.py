@@ -82,8 +82,7 @@ def _worker(rank, world, port, T, combine, skew_zero_rank, result_dir):
     dist.destroy_process_group()
 
 
-def _run(tmp_path, T, combine, skew_zero_rank=False):
-    world = 2
+def _run(tmp_path, T, combine, skew_zero_rank=False, world=2):
     mp.start_processes(_worker, args=(world, _free_port(), T, combine, skew_zero_rank, str(tmp_path)),
                        nprocs=world, start_method="spawn", join=True)
     return [torch.load(os.path.join(tmp_path, f"r{r}.pt")) for r in range(world)]
@@ -108,6 +107,20 @@ def test_ep_bf16_combine_and_empty_rank(tmp_path):
     for r in res:
         torch.testing.assert_close(r["out"].float(), r["full"].to(torch.bfloat16).float(), rtol=1e-2, atol=1e-2)
     assert res[0]["send"][1] == 0 and res[1]["send"][1] == 0  # nobody routes to rank 1's experts
+
+
+@pytest.mark.timeout(300)
+def test_ep_four_ranks(tmp_path):
+    """4 ranks (64 experts each): every rank's output equals the
+    single-process layer, and the send/recv matrix is consistent."""
+    world = 4
+    res = _run(tmp_path, 20, "f32", world=world)
+    for r in res:
+        torch.testing.assert_close(r["out"].float(), r["full"].to(torch.bfloat16).float(), rtol=1e-2, atol=1e-2)
+    for a in range(world):
+        for b in range(world):
+            assert res[a]["send"][b] == res[b]["recv"][a]
+    assert sum(sum(r["send"]) for r in res) > 0
 
 
 def test_pack_unpack_round_trip():
