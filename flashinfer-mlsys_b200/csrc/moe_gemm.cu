@@ -589,13 +589,19 @@ size_t gemm_smem_bytes() { return kRingBytes + sizeof(SmemCtl) + 1024; }
 template <int kMode, int kSkinny>
 cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
                         const float* w_scale, cudaStream_t s, int plan_early) {
-  static int configured = 0;
+  // The shared-memory opt-in is a per-device function attribute: one bit per
+  // device that has it (launches run under the library's host mutex).
+  static uint64_t configured = 0;
   const size_t smem = gemm_smem_bytes();
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<kMode, kSkinny>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0;
+  if (!(configured & bit) || !bit) {
+    e = cudaFuncSetAttribute(moe_gemm_kernel<kMode, kSkinny>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    configured = 1;
+    configured |= bit;
   }
   const int sms = device_sm_count();
   GemmArgs p{};

@@ -117,6 +117,26 @@ def test_repeated_and_resized_calls(gpu_available):
     assert diff <= 1e-2 * max(1.0, o1.float().abs().max().item())
 
 
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_devices_in_one_process(gpu_available):
+    """One process drives the layer on two GPUs in turn: per-device workspace,
+    launch attributes and tensor maps."""
+    O = oracle()
+    acts = workloads().config_activations(8)
+    outs = []
+    for d in (0, 1, 0):
+        dev = torch.device("cuda", d)
+        with torch.cuda.device(dev):
+            w = workloads().make_weights(32, 0, dev, weight_seed=0)
+            out, ids, _, cnt = run_gpu(acts.to(dev), w)
+        outs.append((out.cpu(), ids.cpu(), cnt.cpu()))
+    ref = O.moe_forward(acts.logits.numpy(), O.as_f32(acts.bias), O.as_u8(acts.hidden), acts.hidden_scale.numpy(),
+                        lambda le: w.expert_cpu(le), 0, 2.5, 32)
+    for out, ids, cnt in outs:
+        check_output(out, ref["out_f32"])
+        assert torch.equal(ids, outs[0][1]) and torch.equal(cnt, outs[0][2])
+
+
 def test_route_entry(gpu_available):
     m = pkg()
     acts = workloads().make_activations(300, seed=3)
