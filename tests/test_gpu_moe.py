@@ -74,6 +74,64 @@ def test_parity_skewed_prefill_subset(gpu_available, T):
     check_output(out, ref["out_f32"], rows=rows)
 
 
+def test_parity_beyond_benchmark_sizes_T65536(gpu_available):
+    """Four times the largest benchmark call (near-uniform routing, ~16k
+    local rows, a 13.5 GB workspace): 64-bit indexing of rows, scales and
+    routing CTAs. Full routing/counts; output on a token subset. The
+    workspace is released afterwards."""
+    T = 65536
+    acts = workloads().make_activations(T, seed=11)
+    w = gpu_weights()
+    out, ids, wts, cnt = run_gpu(acts.to(DEV), w)
+    O = oracle()
+    routing = O.route(acts.logits.numpy(), O.as_f32(acts.bias), 2.5)
+    check_routing(routing, ids, cnt, 0, 32)
+    rng = np.random.default_rng(T)
+    rows = np.sort(np.concatenate([rng.choice(T, size=20, replace=False), [0, T - 1]]))
+    ref = oracle_run(acts, w, token_subset=rows)
+    check_output(out, ref["out_f32"], rows=rows)
+    del out
+    pkg().load().moe_fp8_ds_release_workspace()
+    torch.cuda.empty_cache()
+
+
+def test_cuda_graph_capture_and_replay(gpu_available):
+    """The layer is graph-capturable once its workspace is sized: no host
+    synchronisation or allocation inside the call. Replays on new input
+    contents give the direct call's results."""
+    m = pkg()
+    w = gpu_weights()
+    srcs = [workloads().config_activations(8).to(DEV), workloads().make_activations(8, seed=99).to(DEV)]
+    refs = [run_gpu(x, w)[0] for x in srcs]
+    st = workloads().make_activations(8, seed=1).to(DEV)   # static input buffers of the graph
+    out = torch.empty((8, 7168), dtype=torch.bfloat16, device=DEV)
+
+    def call():
+        m.kernel(st.logits, st.bias, st.hidden, st.hidden_scale, w.w13, w.s13, w.w2, w.s2, 0, 2.5, out)
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        call()
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        call()
+    for _ in range(2):
+        for x, ref in zip(srcs, refs):
+            for d, s_ in ((st.logits, x.logits), (st.bias, x.bias), (st.hidden, x.hidden),
+                          (st.hidden_scale, x.hidden_scale)):
+                d.copy_(s_)
+            out.fill_(float("nan"))
+            g.replay()
+            torch.cuda.synchronize()
+            diff = (out.float() - ref.float()).abs()
+            assert torch.isfinite(out.float()).all()
+            assert diff.max().item() <= 1e-2 * max(1.0, ref.float().abs().max().item())
+    assert m.device_status() == 0
+    del g
+
+
 def test_no_local_tokens_gives_zero_output(gpu_available):
     acts = workloads().make_activations(16, seed=5)
     bias = acts.bias.float()
