@@ -7,6 +7,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import threading
 
 from . import build as _build
 
@@ -43,6 +44,7 @@ SIGNATURES = {
 }
 
 _lib = None
+_load_lock = threading.Lock()
 
 
 def lib_path() -> str:
@@ -52,21 +54,25 @@ def lib_path() -> str:
 
 
 def load(build_if_missing: bool = True) -> ctypes.CDLL:
-    """Load (building first if needed) the sm_100a library and bind signatures."""
+    """Load (building first if needed) the sm_100a library and bind signatures.
+    Thread-safe: concurrent first calls build and load once."""
     global _lib
     if _lib is not None:
         return _lib
-    path = lib_path()
-    if path == _build.LIB_PATH and (not os.path.exists(path) or (build_if_missing and _build.is_stale())):
-        if not build_if_missing:
-            raise RuntimeError(f"{path} is missing: run `python -m` build (flashinfer-mlsys_b200/build.py)")
-        _build.build()
-    lib = ctypes.CDLL(path)
-    for name, (res, args) in SIGNATURES.items():
-        fn = getattr(lib, name)
-        fn.restype = res
-        fn.argtypes = args
-    _lib = lib
+    with _load_lock:
+        if _lib is not None:
+            return _lib
+        path = lib_path()
+        if path == _build.LIB_PATH and (not os.path.exists(path) or (build_if_missing and _build.is_stale())):
+            if not build_if_missing:
+                raise RuntimeError(f"{path} is missing: build it with `python flashinfer-mlsys_b200/build.py`")
+            _build.build()
+        lib = ctypes.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
     return lib
 
 

@@ -71,7 +71,7 @@ _VALID_WEIGHTS: dict = {}
 
 def _weights_ok(w1, s1, w2, s2, e_local, dev):
     key = (id(w1), id(s1), id(w2), id(s2))
-    sig = (w1.data_ptr(), s1.data_ptr(), w2.data_ptr(), s2.data_ptr(), e_local, dev)
+    sig = (e_local, dev) + tuple((t.data_ptr(), t.dtype, tuple(t.shape), t.stride()) for t in (w1, s1, w2, s2))
     if _VALID_WEIGHTS.get(key) == sig:
         return
     _check_weights(w1, s1, w2, s2, e_local)

@@ -54,6 +54,7 @@ def pack_rows(hidden: torch.Tensor, hidden_scale: torch.Tensor, ids: torch.Tenso
     buf = torch.empty((n, ROW_BYTES), dtype=torch.uint8, device=hidden.device)
     if hidden.is_cuda:
         idx64 = idx.to(torch.int64).contiguous()
+        hidden, hidden_scale = hidden.contiguous(), hidden_scale.contiguous()
         _lib_call("moe_fp8_ds_ep_pack", hidden.device, hidden.data_ptr(), hidden_scale.data_ptr(),
                   ids.contiguous().data_ptr(), w.contiguous().data_ptr(), hidden.shape[0], idx64.data_ptr(), n,
                   buf.data_ptr())
