@@ -41,6 +41,7 @@ SIGNATURES = {
     "moe_fp8_ds_ep_pack": (ctypes.c_int, [_vp, _vp, _vp, _vp, _c_int64, _vp, _c_int64, _vp, _vp]),
     "moe_fp8_ds_ep_unpack": (ctypes.c_int, [_vp, _c_int64, _vp, _vp, _vp, _vp, _vp]),
     "moe_fp8_ds_ep_combine": (ctypes.c_int, [_vp, _vp, _c_int64, _c_int64, _vp, _vp]),
+    "moe_fp8_ds_ep_plan": (ctypes.c_int, [_vp, _c_int64, _c_int64, _vp, _vp, _vp, _vp]),
 }
 
 _lib = None

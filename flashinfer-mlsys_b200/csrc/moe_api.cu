@@ -455,6 +455,21 @@ int moe_fp8_ds_ep_unpack(const void* recv_buf, int64_t num_rows, void* hidden_st
   return MOE_OK;
 }
 
+int moe_fp8_ds_ep_plan(const int32_t* topk_ids, int64_t seq_len, int64_t world, int64_t* send_idx,
+                       int64_t* send_counts, int32_t* row_of, void* stream) {
+  if (seq_len < 0 || seq_len > (int64_t(1) << 24) || world < 1 || world > 64 || (kExperts % world) != 0)
+    return MOE_ERR_INVALID_ARG;
+  if (!send_counts) return MOE_ERR_INVALID_ARG;
+  if (seq_len > 0 && (!topk_ids || !send_idx || !row_of)) return MOE_ERR_INVALID_ARG;
+  int rc = check_device();
+  if (rc) return rc;
+  // seq_len 0 still writes the (zero) counts
+  if (launch_ep_plan(topk_ids, static_cast<int>(seq_len), static_cast<int>(world), send_idx, send_counts, row_of,
+                     static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  return MOE_OK;
+}
+
 int moe_fp8_ds_ep_combine(const void* partials, const int32_t* row_of, int64_t seq_len, int64_t world, void* output,
                           void* stream) {
   if (seq_len < 0 || seq_len > (int64_t(1) << 24) || world < 1 || world > 64) return MOE_ERR_INVALID_ARG;

@@ -95,7 +95,95 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// The dispatch plan of one layer call, in one CTA. Rank q owns experts
+// [q*e_local, (q+1)*e_local). For every q, the tokens with at least one
+// expert there, in ascending token order, concatenated rank after rank
+// (send_idx), the count per rank (send_counts) and row_of[t][q] = the row of
+// token t in that concatenation (-1: nothing sent to q). Pass 1 counts with
+// shared-memory atomics; pass 2 places 1024 tokens at a time with a ballot
+// scan per rank, so positions ascend with the token index.
+constexpr int kPlanThreads = 1024;
+__global__ void __launch_bounds__(kPlanThreads)
+    ep_plan_kernel(const int32_t* __restrict__ ids, int T, int world, int64_t* __restrict__ send_idx,
+                   int64_t* __restrict__ send_counts, int32_t* __restrict__ row_of) {
+  __shared__ int cnt[64], off[64], running[64];
+  __shared__ int warp_tot[kPlanThreads / 32], warp_pre[kPlanThreads / 32], chunk_tot;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int e_local = kExperts / world;
+  if (tid < world) cnt[tid] = running[tid] = 0;
+  __syncthreads();
+  auto dest_mask = [&](int t) -> uint64_t {
+    uint64_t m = 0;
+    if (t < T) {
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k) {
+        int q = __ldg(ids + (size_t)t * kTopK + k) / e_local;
+        q = q < 0 ? 0 : (q >= world ? world - 1 : q);
+        m |= 1ull << q;
+      }
+    }
+    return m;
+  };
+  for (int t = tid; t < T; t += kPlanThreads) {
+    uint64_t m = dest_mask(t);
+    while (m) {
+      const int q = __ffsll(static_cast<long long>(m)) - 1;
+      m &= m - 1;
+      atomicAdd(&cnt[q], 1);
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int o = 0;
+    for (int q = 0; q < world; ++q) {
+      off[q] = o;
+      o += cnt[q];
+      send_counts[q] = cnt[q];
+    }
+  }
+  __syncthreads();
+  const unsigned lt = (1u << lane) - 1u;
+  for (int base = 0; base < T; base += kPlanThreads) {
+    const int t = base + tid;
+    const uint64_t m = dest_mask(t);
+    for (int q = 0; q < world; ++q) {
+      const bool f = (m >> q) & 1ull;
+      const unsigned bal = __ballot_sync(0xffffffffu, f);
+      if (lane == 0) warp_tot[warp] = __popc(bal);
+      __syncthreads();
+      if (warp == 0) {
+        const int v = warp_tot[lane];
+        int incl = v;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, d);
+          if (lane >= d) incl += y;
+        }
+        warp_pre[lane] = incl - v;
+        if (lane == 31) chunk_tot = incl;
+      }
+      __syncthreads();
+      if (t < T) {
+        int r = -1;
+        if (f) {
+          r = off[q] + running[q] + warp_pre[warp] + __popc(bal & lt);
+          send_idx[r] = t;
+        }
+        row_of[(size_t)t * world + q] = r;
+      }
+      __syncthreads();
+      if (tid == 0) running[q] += chunk_tot;
+    }
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_ep_plan(const int32_t* ids, int T, int world, int64_t* send_idx, int64_t* send_counts,
+                           int32_t* row_of, cudaStream_t s) {
+  return launch_k(ep_plan_kernel, dim3(1), dim3(kPlanThreads), 0, s, false, ids, T, world, send_idx, send_counts,
+                  row_of);
+}
 
 cudaError_t launch_ep_pack(const void* hidden, const float* hidden_scale, const int32_t* ids, const float* w, int T,
                            const int64_t* idx, int S, void* out, cudaStream_t s) {

@@ -142,6 +142,8 @@ cudaError_t launch_ep_pack(const void* hidden, const float* hidden_scale, const 
 cudaError_t launch_ep_unpack(const void* in, int R, void* hidden, float* hidden_scale, int32_t* ids, float* w,
                              cudaStream_t s);
 cudaError_t launch_ep_combine(const void* back, const int32_t* row_of, int T, int world, void* out, cudaStream_t s);
+cudaError_t launch_ep_plan(const int32_t* ids, int T, int world, int64_t* send_idx, int64_t* send_counts,
+                           int32_t* row_of, cudaStream_t s);
 
 // BF16 [T][7168] -> e4m3 [T][7168] + f32 scales [56][T] (1x128 blocks, amax / 448)
 cudaError_t launch_quant_rows(const void* x, int T, void* q, float* scale, cudaStream_t s);

@@ -19,9 +19,9 @@ call:
 The route and expert functions are parameters, so the same bookkeeping runs
 with the CUDA library on GPUs (NCCL) and with CPU functions under a gloo
 process group in the tests. On CUDA tensors the row packing, unpacking and
-the combine are the library's kernels (moe_fp8_ds_ep_pack / _unpack /
-_combine); the torch expressions below are their CPU restatement for the
-gloo tests.
+the combine, and the dispatch plan, are the library's kernels
+(moe_fp8_ds_ep_pack / _unpack / _combine / _plan); the torch expressions
+below are their CPU restatement for the gloo tests.
 """
 from __future__ import annotations
 
@@ -92,12 +92,13 @@ class Plan:
     send_idx: torch.Tensor      # token index of every sent row, grouped by destination rank
     send_counts: list           # rows sent to each rank
     recv_counts: list           # rows received from each rank
+    row_of: Optional[torch.Tensor] = None  # int32 [T, world]: row of token t in send_idx for rank q, -1 if none
 
 
-def dispatch_plan(ids: torch.Tensor, world: int, group=None) -> Plan:
-    """Which tokens go to which rank (once per rank, ascending token order),
-    and the exchange of the per-rank row counts. One host synchronisation:
-    NCCL's all-to-all-v takes its split sizes on the host."""
+def plan_local(ids: torch.Tensor, world: int):
+    """The local half of the dispatch plan in torch (the restatement of the
+    moe_fp8_ds_ep_plan kernel): (send order int64 [world*T] with the first
+    sum(counts) valid, counts int64 [world], row_of int32 [T, world])."""
     e_local = E_GLOBAL // world
     T = ids.shape[0]
     dest = torch.zeros((world, T), dtype=torch.bool, device=ids.device)
@@ -111,12 +112,36 @@ def dispatch_plan(ids: torch.Tensor, world: int, group=None) -> Plan:
     pos = torch.where(flat, torch.cumsum(flat, 0) - 1, torch.full_like(flat, n, dtype=torch.int64))
     order = torch.empty(n + 1, dtype=torch.int64, device=ids.device)
     order.scatter_(0, pos, torch.arange(n, device=ids.device) % T)
-    send_counts_t = dest.sum(dim=1).to(torch.int64)
+    counts = dest.sum(dim=1).to(torch.int64)
+    row_of = torch.full((T, world), -1, dtype=torch.int32, device=ids.device)
+    rows = torch.where(flat, torch.cumsum(flat, 0) - 1, torch.full_like(flat, -1, dtype=torch.int64))
+    row_of.copy_(rows.view(world, T).t().to(torch.int32))
+    return order[:n], counts, row_of
+
+
+def plan_cuda(ids: torch.Tensor, world: int):
+    """plan_local's triple from the moe_fp8_ds_ep_plan kernel (one launch)."""
+    dev = ids.device
+    T = ids.shape[0]
+    order = torch.empty(max(world * T, 1), dtype=torch.int64, device=dev)
+    counts = torch.empty(world, dtype=torch.int64, device=dev)
+    row_of = torch.empty((T, world), dtype=torch.int32, device=dev)
+    ids32 = ids.to(torch.int32).contiguous()
+    _lib_call("moe_fp8_ds_ep_plan", dev, ids32.data_ptr() if T else None, T, world, order.data_ptr(),
+              counts.data_ptr(), row_of.data_ptr() if T else None)
+    return order, counts, row_of
+
+
+def dispatch_plan(ids: torch.Tensor, world: int, group=None) -> Plan:
+    """Which tokens go to which rank (once per rank, ascending token order),
+    and the exchange of the per-rank row counts. One host synchronisation:
+    NCCL's all-to-all-v takes its split sizes on the host."""
+    order, send_counts_t, row_of = plan_cuda(ids, world) if ids.is_cuda else plan_local(ids, world)
     recv_counts_t = torch.empty_like(send_counts_t)
     dist.all_to_all_single(recv_counts_t, send_counts_t, group=group)
     both = torch.cat([send_counts_t, recv_counts_t]).tolist()
     send_counts, recv_counts = both[:world], both[world:]
-    return Plan(order[:sum(send_counts)], send_counts, recv_counts)
+    return Plan(order[:sum(send_counts)], send_counts, recv_counts, row_of)
 
 
 def ep_forward(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden: torch.Tensor,
@@ -159,11 +184,13 @@ def combine_rows(back: torch.Tensor, plan: Plan, T: int, world: int) -> torch.Te
     if back.is_cuda and back.dtype == torch.bfloat16:
         dev = back.device
         # row_of[t][q]: the row of token t in the block returned by rank q, -1 if none
-        row_of = torch.full((T, world), -1, dtype=torch.int32, device=dev)
-        if plan.send_idx.numel():
-            q = torch.repeat_interleave(torch.arange(world, device=dev),
-                                        torch.tensor(plan.send_counts, device=dev))
-            row_of[plan.send_idx, q] = torch.arange(plan.send_idx.numel(), dtype=torch.int32, device=dev)
+        row_of = plan.row_of
+        if row_of is None:
+            row_of = torch.full((T, world), -1, dtype=torch.int32, device=dev)
+            if plan.send_idx.numel():
+                q = torch.repeat_interleave(torch.arange(world, device=dev),
+                                            torch.tensor(plan.send_counts, device=dev))
+                row_of[plan.send_idx, q] = torch.arange(plan.send_idx.numel(), dtype=torch.int32, device=dev)
         out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
         _lib_call("moe_fp8_ds_ep_combine", dev, back.data_ptr() if back.numel() else None, row_of.data_ptr(), T,
                   world, out.data_ptr())

@@ -206,12 +206,21 @@ int moe_fp8_ds_add_norm_quant(const void* x_bf16, void* residual_bf16, const voi
  * moe_fp8_ds_ep_combine: output bf16 [seq_len][7168], output[t] = sum over
  *   q = 0..world-1 of partials[row_of[t][q]] (bf16 rows, -1 = none) in fp32 in
  *   rank order, cast once.
+ * moe_fp8_ds_ep_plan: the dispatch plan from topk_ids int32 [seq_len][8]
+ *   (global expert ids) for `world` ranks (1..64, dividing 256; rank q owns
+ *   experts [q*256/world, (q+1)*256/world)). send_counts int64 [world]:
+ *   tokens with at least one expert on rank q. send_idx int64 [world*seq_len]
+ *   (first sum(send_counts) written): those tokens, ascending, rank after rank.
+ *   row_of int32 [seq_len][world]: the row of token t in send_idx for rank q,
+ *   -1 if none (the combine's input).
  */
 int moe_fp8_ds_ep_pack(const void* hidden_states, const float* hidden_states_scale, const int32_t* topk_ids,
                        const float* topk_weights, int64_t seq_len, const int64_t* send_idx, int64_t num_send,
                        void* send_buf, void* stream);
 int moe_fp8_ds_ep_unpack(const void* recv_buf, int64_t num_rows, void* hidden_states, float* hidden_states_scale,
                          int32_t* topk_ids, float* topk_weights, void* stream);
+int moe_fp8_ds_ep_plan(const int32_t* topk_ids, int64_t seq_len, int64_t world, int64_t* send_idx,
+                       int64_t* send_counts, int32_t* row_of, void* stream);
 int moe_fp8_ds_ep_combine(const void* partials, const int32_t* row_of, int64_t seq_len, int64_t world, void* output,
                           void* stream);
 

@@ -134,3 +134,25 @@ def test_pack_unpack_round_trip():
     assert torch.equal(h.view(torch.uint8), a.hidden.view(torch.uint8)[idx])
     assert torch.equal(s, a.hidden_scale[:, idx])
     assert torch.equal(i, ids[idx]) and torch.equal(ww, w[idx])
+
+
+def test_plan_local_row_map_matches_send_order():
+    """The torch restatement of the dispatch-plan kernel: row_of[t][q] is the
+    position of token t in the send order for rank q, and the send order lists
+    each rank's tokens ascending."""
+    ep = importlib.import_module("flashinfer-mlsys_b200.ep")
+    g = torch.Generator().manual_seed(3)
+    for world in (1, 2, 4, 8):
+        ids = torch.stack([torch.randperm(256, generator=g)[:8] for _ in range(50)]).to(torch.int32)
+        order, counts, row_of = ep.plan_local(ids, world)
+        total = int(counts.sum())
+        off = 0
+        for q in range(world):
+            n = int(counts[q])
+            toks = order[off:off + n]
+            assert torch.all(toks[1:] > toks[:-1])
+            want = ((ids.long() // (256 // world)) == q).any(dim=1).nonzero().flatten()
+            assert torch.equal(toks, want)
+            assert torch.equal(row_of[toks, q].long(), torch.arange(off, off + n))
+            off += n
+        assert off == total and int((row_of >= 0).sum()) == total
