@@ -205,24 +205,6 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                : "memory");
 }
 
-// 32 lanes x 32 consecutive 32-bit columns: thread i of the warp receives row
-// (lane base + i), columns [col, col+32). Waits for completion.
-__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 // 32 lanes x 16 consecutive 32-bit columns: thread i of the warp receives row
 // (lane base + i), columns [col, col+16). Waits for completion.
 __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float (&v)[16]) {
@@ -293,10 +275,6 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
                : "memory");
 }
 
-__device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-
 // e4m3 conversion of two floats (round to nearest even, saturating).
 __device__ __forceinline__ uint16_t f2_to_e4m3x2(float lo, float hi) {
   uint16_t r;
@@ -304,15 +282,6 @@ __device__ __forceinline__ uint16_t f2_to_e4m3x2(float lo, float hi) {
       : "=h"(r)
       : "f"(lo), "f"(hi));
   return r;
-}
-__device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
-  // exact decode of one e4m3 byte via the packed converter
-  uint16_t in = b;
-  uint32_t h2;
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(in));
-  __half_raw hr;
-  hr.x = static_cast<unsigned short>(h2 & 0xFFFFu);
-  return __half2float(__half(hr));
 }
 
 }  // namespace moe
