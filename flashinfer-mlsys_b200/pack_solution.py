@@ -12,15 +12,18 @@ The spec fields follow the harness's documented solution format
 (README.md:236-279: DPS on by default, binding "torch" or "tvm-ffi"); the
 reference's own packer sets no binding (scripts/pack_solution.py:56-62), which
 its notes say the torch extension needs (notes/cuda_changes_and_plan.md:5-18).
-Sources are flat: ``kernel.cu`` (the torch-binding entry, solution/kernel.cu of
-this package), every .cu/.cuh/.h of csrc/ and the C-ABI header moe_fp8_ds.h.
-The harness's builder compiles every .cu of the directory; it must pass
-``-gencode arch=compute_100a,code=sm_100a`` (the kernels use tcgen05 and TMA).
+Sources are flat: ``kernel.cu`` (the entry of the chosen binding: this
+package's solution/kernel.cu for "torch", solution/kernel_tvm_ffi.cu for
+"tvm-ffi"), every .cu/.cuh/.h of csrc/ and the C-ABI header moe_fp8_ds.h.
+The harness's builder compiles every .cu of the directory and must target
+sm_100a only (the kernels use tcgen05 and TMA): ``-gencode
+arch=compute_100a,code=sm_100a``, which for tvm_ffi's builder means
+TVM_FFI_CUDA_ARCH_LIST="10.0a".
 
 flashinfer_bench itself (third-party, not vendored by the reference) is not
 needed to write or read the document.
 
-    python -m flashinfer-mlsys_b200.pack_solution [-o solution.json] [--name N] [--author A]
+    python -m flashinfer-mlsys_b200.pack_solution [-o solution.json] [--name N] [--author A] [--binding torch|tvm-ffi]
 """
 from __future__ import annotations
 
@@ -33,19 +36,22 @@ from . import build as _build
 DEFINITION = "moe_fp8_block_scale_ds_routing_topk8_ng8_kg4_e32_h7168_i2048"
 ENTRY_FILE = "kernel.cu"
 HERE = os.path.dirname(os.path.abspath(__file__))
+ENTRY_SOURCES = {"torch": "kernel.cu", "tvm-ffi": "kernel_tvm_ffi.cu"}
 
 
-def source_files() -> list[tuple[str, str]]:
+def source_files(binding: str = "torch") -> list[tuple[str, str]]:
     """(path inside the solution, file on disk), entry point first."""
-    files = [(ENTRY_FILE, os.path.join(HERE, "solution", ENTRY_FILE))]
+    if binding not in ENTRY_SOURCES:
+        raise ValueError(f"binding must be one of {sorted(ENTRY_SOURCES)}, got {binding!r}")
+    files = [(ENTRY_FILE, os.path.join(HERE, "solution", ENTRY_SOURCES[binding]))]
     files += [(f, os.path.join(_build.CSRC, f)) for f in _build.SOURCES + _build.HEADERS]
     files.append(("moe_fp8_ds.h", os.path.join(_build.INCLUDE, "moe_fp8_ds.h")))
     return files
 
 
-def pack(name: str = "moe-fp8-ds-b200", author: str = "flashinfer-mlsys_b200") -> dict:
+def pack(name: str = "moe-fp8-ds-b200", author: str = "flashinfer-mlsys_b200", binding: str = "torch") -> dict:
     sources = []
-    for path, disk in source_files():
+    for path, disk in source_files(binding):
         with open(disk, encoding="utf-8") as f:
             sources.append({"path": path, "content": f.read()})
     return {
@@ -58,7 +64,7 @@ def pack(name: str = "moe-fp8-ds-b200", author: str = "flashinfer-mlsys_b200") -
             "entry_point": f"{ENTRY_FILE}::kernel",
             "dependencies": [],
             "destination_passing_style": True,
-            "binding": "torch",
+            "binding": binding,
         },
         "sources": sources,
     }
@@ -87,8 +93,9 @@ def main() -> None:
     ap.add_argument("-o", "--output", default="solution.json")
     ap.add_argument("--name", default="moe-fp8-ds-b200")
     ap.add_argument("--author", default="flashinfer-mlsys_b200")
+    ap.add_argument("--binding", default="torch", choices=sorted(ENTRY_SOURCES))
     args = ap.parse_args()
-    sol = pack(args.name, args.author)
+    sol = pack(args.name, args.author, args.binding)
     with open(args.output, "w", encoding="utf-8") as f:
         json.dump(sol, f, indent=2)
     print(f"Solution packed: {args.output} ({len(sol['sources'])} sources, entry {sol['spec']['entry_point']})")

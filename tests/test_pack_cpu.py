@@ -51,3 +51,24 @@ def test_extracted_tree_compiles_flat(tmp_path):
     bad = subprocess.run([nvcc, "-gencode", "arch=compute_100,code=sm_100", "-std=c++17", "-I", str(tmp_path),
                           "-c", src, "-o", str(tmp_path / "b.o")], capture_output=True, text=True)
     assert bad.returncode != 0 and "sm_100a" in bad.stderr
+
+
+def test_tvm_ffi_binding_entry(tmp_path):
+    """binding "tvm-ffi": the entry kernel.cu is the TVM-FFI export of the
+    same operator, and it compiles flat against tvm_ffi's headers."""
+    sol = pack.pack(binding="tvm-ffi")
+    assert sol["spec"]["binding"] == "tvm-ffi" and sol["spec"]["entry_point"] == "kernel.cu::kernel"
+    entry = next(s["content"] for s in sol["sources"] if s["path"] == "kernel.cu")
+    assert "TVM_FFI_DLL_EXPORT_TYPED_FUNC(kernel" in entry and "PYBIND11_MODULE" not in entry
+    with pytest.raises(ValueError):
+        pack.pack(binding="tvm")
+    tvm_ffi = pytest.importorskip("tvm_ffi")
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(nvcc):
+        pytest.skip("nvcc not available")
+    pack.extract(sol, str(tmp_path))
+    inc = os.path.join(os.path.dirname(tvm_ffi.__file__), "include")
+    r = subprocess.run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-std=c++17", "-I", str(tmp_path),
+                        "-I", inc, "-c", str(tmp_path / "kernel.cu"), "-o", str(tmp_path / "k.o")],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]
