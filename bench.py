@@ -4,12 +4,17 @@ Default (N=1): BASELINE configs[1], the decode sweep T in {1,2,4,8,16,32,64}
 on one B200 with 32 local experts (offset 0, scaling 2.5). One step = one
 layer call at every T of the sweep; `value` = mean microseconds per call
 (device time from CUDA events around each call, the L2 flushed with a 256 MB
-write before every call, outside the events). `--workload mid|large` runs
-configs[2] / configs[3] instead.
+write before every call, outside the events). Other workloads:
+- `--workload mid|large`: configs[2] / configs[3];
+- `--workload ep` (the default under torchrun with N > 1): configs[4], the full
+  256-expert layer with expert parallelism, 4096 tokens per GPU;
+- `--workload quant|addnorm`: the steps either side of the layer.
 
 `--impl reference` times the reference algorithm on the host CPU cores (the
 numpy restatement in oracle/, because the reference is Python/PyTorch and
 cannot be compiled into oracle/_ref), one sweep point per step.
+`--impl flashinfer` times FlashInfer's fused FP8 block-scale MoE on the same
+inputs (a library comparator, not the reference).
 """
 from __future__ import annotations
 
