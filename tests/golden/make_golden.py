@@ -3,7 +3,9 @@
 
 Run in a container where the reference checkout is present:
 
-    python tests/golden/make_golden.py /path/to/reference
+    python tests/golden/make_golden.py /path/to/reference [case ...]
+
+(all cases by default; naming cases regenerates only those).
 
 Inputs are regenerated from seeds by ``flashinfer-mlsys_b200/workloads.py``
 (CPU generators, so the bytes are reproducible on any machine with the same
@@ -36,6 +38,12 @@ CASES = {
     "decode_T64": (64, 64, 0, None),
     "skew_T32": (32, 32, 0, (0, 1, 2, 3)),
     "offset224_T16": (16, 16, 224, None),
+    # token counts and expert offsets of the contest's workloads (T in
+    # {1, 7, 14, 15, 16, 32, 52-59, 62, 80, ...}, offsets multiples of 32)
+    "contest_T7_off96": (7, 7, 96, None),
+    "contest_T15_off32": (15, 15, 32, None),
+    "contest_T55_off160": (55, 55, 160, None),
+    "contest_T80_off192": (80, 80, 192, None),
 }
 SCALE = 2.5
 E_LOCAL = 32
@@ -85,11 +93,13 @@ def run_reference(ref, a: "wl.Activations", w: "wl.Weights"):
     return out, topk_idx
 
 
-def main(ref_root: str) -> None:
+def main(ref_root: str, names=None) -> None:
     torch.set_num_threads(os.cpu_count() or 1)
     ref = load_reference(ref_root)
     weights = {}
     for name, (T, seed, offset, hot) in CASES.items():
+        if names and name not in names:
+            continue
         if offset not in weights:
             t0 = time.time()
             weights[offset] = wl.make_weights(E_LOCAL, offset, "cpu", weight_seed=0)
@@ -116,4 +126,4 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", sys.argv[2:])
