@@ -47,6 +47,22 @@ WORKLOADS = {
 L2_FLUSH_BYTES = 256 << 20
 
 
+def _host_info() -> dict:
+    """The host the CPU arms ran on: CPU model and the numerics libraries."""
+    import numpy as np
+
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"cpu_model": model, "numpy": np.__version__}
+
+
 def _peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -433,7 +449,8 @@ def cpu_baseline(Ts, acts, w):
         _oracle_call(O, acts[T], get_expert)
         times.append(time.perf_counter() - t0)
     return {"value": round(statistics.mean(times) * 1e6, 1), "unit": "us/call", "cores": os.cpu_count(),
-            "kind": "port", "sample": f"one oracle call at each T in {sample} (numpy, BLAS on all cores)"}
+            "kind": "port", "sample": f"one oracle call at each T in {sample} (numpy, BLAS on all cores)",
+            **_host_info()}
 
 
 def bench_reference(args):
@@ -490,7 +507,7 @@ def bench_reference(args):
         "config": {"workload": f"{args.workload}: {wdesc}", "T": list(Ts), "num_local_experts": e_local,
                    "local_expert_offset": 0, "routed_scaling_factor": 2.5},
         "cpu_baseline": {"value": round(us, 1), "unit": "us/call", "cores": os.cpu_count(), "kind": "port",
-                         "sample": sample},
+                         "sample": sample, **_host_info()},
         "e2e": {"value": round(us, 1), "unit": "us/call", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
