@@ -110,10 +110,10 @@ def test_ep_bf16_combine_and_empty_rank(tmp_path):
 
 
 @pytest.mark.timeout(300)
-def test_ep_four_ranks(tmp_path):
-    """4 ranks (64 experts each): every rank's output equals the
+@pytest.mark.parametrize("world", [4, 8])
+def test_ep_four_and_eight_ranks(tmp_path, world):
+    """4 and 8 ranks (64 / 32 experts each): every rank's output equals the
     single-process layer, and the send/recv matrix is consistent."""
-    world = 4
     res = _run(tmp_path, 20, "f32", world=world)
     for r in res:
         torch.testing.assert_close(r["out"].float(), r["full"].to(torch.bfloat16).float(), rtol=1e-2, atol=1e-2)
