@@ -70,14 +70,15 @@ extern "C" int moe_fp8_ds_route_noalloc(const float* routing_logits, const void*
     return MOE_ERR_INVALID_ARG;
   if (local_expert_offset < -(int64_t(1) << 30) || local_expert_offset > (int64_t(1) << 30))
     return MOE_ERR_INVALID_ARG;
-  if (seq_len == 0) return MOE_OK;
-  if (!routing_logits || !routing_bias || !topk_ids_out || !topk_weights_out) return MOE_ERR_INVALID_ARG;
-  if ((reinterpret_cast<uintptr_t>(routing_logits) & 15u) || (reinterpret_cast<uintptr_t>(routing_bias) & 15u))
-    return MOE_ERR_ALIGNMENT;
+  // the device check comes first so that empty calls return the same codes as moe_fp8_ds_route
   int major = 0, dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess || major != 10)
     return MOE_ERR_NO_DEVICE;
+  if (seq_len == 0) return MOE_OK;
+  if (!routing_logits || !routing_bias || !topk_ids_out || !topk_weights_out) return MOE_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(routing_logits) & 15u) || (reinterpret_cast<uintptr_t>(routing_bias) & 15u))
+    return MOE_ERR_ALIGNMENT;
   void* base = nullptr;
   int rc = scratch_ptr(&base);
   if (rc) return rc;

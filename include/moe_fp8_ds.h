@@ -109,6 +109,9 @@ int moe_fp8_ds_route(const float* routing_logits, const void* routing_bias,
  * and launch nothing); num_local_experts in {32, 64, 128, 256}.
  * The first call on a device looks up the array's device address (once per
  * device); make that first call before capturing a stream into a CUDA graph.
+ * The address is kept for the life of the process: after the device's primary
+ * context is destroyed (cudaDeviceReset) the array moves, so do not call this
+ * function again in that process.
  * Every call reuses the same array: calls that may run at the same time on the
  * GPU (different streams without ordering, or different host threads) race on
  * it and must be serialised by the caller.

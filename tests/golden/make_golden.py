@@ -126,4 +126,6 @@ def main(ref_root: str, names=None) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", sys.argv[2:])
+    if len(sys.argv) < 2 or not os.path.isdir(sys.argv[1]):
+        sys.exit("usage: python tests/golden/make_golden.py <reference checkout> [case ...]")
+    main(sys.argv[1], sys.argv[2:])

@@ -16,7 +16,8 @@ import importlib
 import pytest
 import torch
 
-from conftest import workloads
+from conftest import oracle, workloads
+from parity import check_routing, check_weights
 
 pytestmark = pytest.mark.gpu
 
@@ -42,14 +43,25 @@ def test_route_noalloc_matches_route_twice(gpu_available):
     lib = pkg.load()
     dev = torch.device("cuda", torch.cuda.current_device())
     stream = torch.cuda.current_stream(dev).cuda_stream
-    cases = [(300, 3, 64, 32), (37, 4, 0, 128)]  # (tokens, seed, local_expert_offset, local experts)
+    # (tokens, seed, local_expert_offset, local experts); 8192 tokens is the
+    # documented limit, where the id, weight and rank arrays fill the static
+    # array, and 256 local experts is the largest expert table
+    cases = [(300, 3, 64, 32), (37, 4, 0, 128), (8192, 5, 0, 256), (8192, 6, 128, 32)]
+    O = oracle()
     for T, seed, offset, e_local in cases:
-        acts = workloads().make_activations(T, seed).to(dev)
+        cpu = workloads().make_activations(T, seed)
+        acts = cpu.to(dev)
         (ids_a, w_a, c_a), (ids_b, w_b, c_b) = _route_both(lib, acts, offset, e_local, 2.5, stream)
         assert torch.equal(ids_a, ids_b)
         assert torch.equal(c_a, c_b)
         torch.testing.assert_close(w_b, w_a, rtol=1e-6, atol=1e-7)
         assert int(c_b.sum()) > 0
+        if T == 8192:
+            # at the limit, also against the CPU oracle: ids and counts exact
+            # (near-ties reported), weights at the chosen ids
+            routing = O.route(cpu.logits.numpy(), O.as_f32(cpu.bias), 2.5)
+            check_routing(routing, ids_b, c_b, offset, e_local)
+            check_weights(routing, ids_b, w_b)
 
 
 def test_route_noalloc_rejects_oversize_without_launch(gpu_available):
