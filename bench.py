@@ -275,14 +275,14 @@ def bench_ours(args):
 
     # per-kernel device times (CUDA events recorded by the library on this stream)
     lib.moe_fp8_ds_profile_enable(1)
-    kern = {T: np.zeros(5) for T in Ts}
-    nkern = {T: 5 for T in Ts}  # 1 when the call is served by the fused decode kernel
-    buf = (ctypes.c_float * 5)()
+    kern = {T: np.zeros(3) for T in Ts}
+    nkern = {T: 3 for T in Ts}  # 1 when the call is served by the fused decode kernel
+    buf = (ctypes.c_float * 3)()
     for s in range(args.steps):
         for T in Ts:
             flush.zero_()
             call(T)
-            n = lib.moe_fp8_ds_profile_last(buf, 5)
+            n = lib.moe_fp8_ds_profile_last(buf, 3)
             nkern[T] = n
             kern[T][:n] += np.array(buf[:n])
     lib.moe_fp8_ds_profile_enable(0)
@@ -344,7 +344,7 @@ def bench_ours(args):
             "roofline_frac": round(t_roof_ms / ms, 4),
             "kernel_us": ({"fused_decode": round(kern[T][0] * 1e3, 2)} if nkern[T] == 1 else
                           {k: round(v * 1e3, 2) for k, v in zip(
-                              ["route", "permute", "gemm1", "gemm2", "finalize"], kern[T])}),
+                              ["route", "gemm1", "gemm2"], kern[T])}),
         }
         tot_flops += flops
         tot_bytes += byts
@@ -356,7 +356,7 @@ def bench_ours(args):
         else:
             g1_bytes += st["e_touched"] * (4096 * 7168 + 32 * 56 * 4) + st["n_assign"] * (7168 + 56 * 4 + 4096 + 64)
             g1_flops += st["n_assign"] * 2 * 7168 * 4096
-            g1_ms += kern[T][2]
+            g1_ms += kern[T][1]
     tot_ms = sum(per_T_ms.values())
     n_calls = len(Ts)
     value = tot_ms * 1e3 / n_calls
