@@ -57,19 +57,44 @@ def test_parity_decode_and_mid(gpu_available, T):
     check_output(out, ref["out_f32"])
 
 
-@pytest.mark.parametrize("T", [4096, 16384])
-def test_parity_skewed_prefill_subset(gpu_available, T):
-    """Full routing/counts; output checked on a token subset (the oracle's cost
-    grows with T, each output row depends only on its own token)."""
+def _rows_covering_every_mtile(T, e_local, counts, n_min, seed):
+    """Tokens whose expert rows together touch every m-tile of every local
+    expert (first, last and partial ones included), from the row placement of
+    the call just made, topped up with random tokens to at least n_min."""
+    le, sl = pkg().last_rows(T, e_local)
+    le, sl = le.cpu().numpy().astype(np.int64), sl.cpu().numpy().astype(np.int64)
+    ok = le >= 0
+    keys = (le * (1 << 20) + sl // 128)[ok]
+    toks = np.broadcast_to(np.arange(T)[:, None], le.shape)[ok]
+    uniq, first = np.unique(keys, return_index=True)
+    n_tiles = int(sum((int(c) + 127) // 128 for c in counts))
+    assert len(uniq) == n_tiles, (len(uniq), n_tiles)
+    rows = set(int(t) for t in toks[first])
+    rng = np.random.default_rng(seed)
+    for t in rng.permutation(T):
+        if len(rows) >= n_min:
+            break
+        rows.add(int(t))
+    return np.array(sorted(rows), dtype=np.int64)
+
+
+@pytest.mark.parametrize("T", [4096, 8192, 16384])
+def test_parity_skewed_prefill_every_mtile(gpu_available, T):
+    """BASELINE configs[3] (4 hot local experts take every token). Routing and
+    per-expert counts in full; the output on >= 512 tokens chosen so that
+    every m-tile of every local expert (each expert's first and last, partial,
+    tile included) contributes to some checked row. The oracle computes only
+    those rows (each output row depends only on its own token)."""
     acts = workloads().config_activations(T)
     w = gpu_weights()
     out, ids, wts, cnt = run_gpu(acts.to(DEV), w)
     O = oracle()
     routing = O.route(acts.logits.numpy(), O.as_f32(acts.bias), 2.5)
     check_routing(routing, ids, cnt, 0, 32)
-    assert int(cnt.sum()) > T  # the 4 hot local experts take every token
-    rng = np.random.default_rng(T)
-    rows = np.sort(rng.choice(T, size=24, replace=False))
+    counts = cnt.cpu().numpy()
+    assert int(counts[:4].min()) > T // 2  # the 4 hot local experts take most tokens
+    rows = _rows_covering_every_mtile(T, 32, counts, 512, T)
+    assert len(rows) >= 512
     ref = oracle_run(acts, w, token_subset=rows)
     check_output(out, ref["out_f32"], rows=rows)
 
