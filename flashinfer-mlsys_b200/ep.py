@@ -144,37 +144,55 @@ def dispatch_plan(ids: torch.Tensor, world: int, group=None) -> Plan:
     return Plan(order[:sum(send_counts)], send_counts, recv_counts, row_of)
 
 
+# Phases of one expert-parallel call, in order (ep_forward's `marks`).
+PHASES = ("route", "plan+counts", "pack", "dispatch", "unpack", "experts", "return", "combine")
+
+
 def ep_forward(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden: torch.Tensor,
                hidden_scale: torch.Tensor, routed_scaling_factor: float,
                route_fn: Callable, experts_fn: Callable, group=None,
-               combine_dtype: torch.dtype = torch.bfloat16, plan_out: Optional[list] = None) -> torch.Tensor:
+               combine_dtype: torch.dtype = torch.bfloat16, plan_out: Optional[list] = None,
+               marks: Optional[Callable] = None) -> torch.Tensor:
     """One expert-parallel MoE layer call on this rank's tokens; returns bf16 [T, 7168].
 
     route_fn(logits, bias, scale) -> (ids int32 [T,8], weights f32 [T,8]) over all 256 experts.
     experts_fn(hidden, scale, ids, weights, local_expert_offset, out) writes
     out [R,7168] (dtype ``combine_dtype``) = sum over this rank's experts.
+    marks(i): called before phase i of PHASES and once more at the end
+    (i = len(PHASES)); the benchmark records CUDA events there.
     """
+    mark = marks if marks is not None else (lambda i: None)
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     e_local = E_GLOBAL // world
     T = hidden.shape[0]
+    mark(0)
     ids, w = route_fn(routing_logits, routing_bias, routed_scaling_factor)
+    mark(1)
     plan = dispatch_plan(ids, world, group)
     if plan_out is not None:
         plan_out.append(plan)
+    mark(2)
     send_buf = pack_rows(hidden, hidden_scale, ids, w, plan.send_idx)
     R = sum(plan.recv_counts)
     recv_buf = torch.empty((R, ROW_BYTES), dtype=torch.uint8, device=hidden.device)
+    mark(3)
     dist.all_to_all_single(recv_buf, send_buf, output_split_sizes=plan.recv_counts,
                            input_split_sizes=plan.send_counts, group=group)
+    mark(4)
     h_r, s_r, ids_r, w_r = unpack_rows(recv_buf)
     out_r = torch.empty((R, H), dtype=combine_dtype, device=hidden.device)
+    mark(5)
     if R:
         experts_fn(h_r, s_r, ids_r, w_r, rank * e_local, out_r)
     back = torch.empty((plan.send_idx.numel(), H), dtype=combine_dtype, device=hidden.device)
+    mark(6)
     dist.all_to_all_single(back, out_r, output_split_sizes=plan.send_counts,
                            input_split_sizes=plan.recv_counts, group=group)
-    return combine_rows(back, plan, T, world)
+    mark(7)
+    out = combine_rows(back, plan, T, world)
+    mark(8)
+    return out
 
 
 def combine_rows(back: torch.Tensor, plan: Plan, T: int, world: int) -> torch.Tensor:

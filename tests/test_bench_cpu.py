@@ -26,3 +26,17 @@ def test_reference_arm_json_line():
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["value"] == d["value"]
     assert "workload" in d["config"]
+
+
+def test_reference_and_our_arm_share_the_config_keys():
+    """The driver compares the two arms' `config`; both build it with the same
+    function, for the default workload at every N and for the T sweep."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    for world in (1, 2, 4, 8):
+        c = bench._config("ep", world, (4096,))
+        assert c["num_local_experts"] == 256 // world and c["T_per_gpu"] == 4096
+        assert c["parallelism"] == f"ep{world}"
+    for name in bench.SWEEP:
+        assert bench._config(name, 1, bench.WORKLOADS[name][0])["T"] == list(bench.WORKLOADS[name][0])
