@@ -328,14 +328,14 @@ def _measure_layer(pkg, lib, dev, stream, flush, w, acts_cpu, e_local, steps, wa
     if kernels:
         # per-kernel device times (CUDA events recorded by the library on this stream)
         lib.moe_fp8_ds_profile_enable(1)
-        kern = {T: np.zeros(3) for T in Ts}
-        nk = {T: 3 for T in Ts}
-        buf = (ctypes.c_float * 3)()
+        kern = {T: np.zeros(5) for T in Ts}
+        nk = {T: 5 for T in Ts}
+        buf = (ctypes.c_float * 5)()
         for _ in range(steps):
             for T in Ts:
                 flush.zero_()
                 call(T)
-                n = lib.moe_fp8_ds_profile_last(buf, 3)
+                n = lib.moe_fp8_ds_profile_last(buf, 5)
                 nk[T] = n
                 kern[T][:n] += np.array(buf[:n])
         lib.moe_fp8_ds_profile_enable(0)
@@ -381,6 +381,17 @@ def _measure_layer(pkg, lib, dev, stream, flush, w, acts_cpu, e_local, steps, wa
     return res
 
 
+# Intervals moe_fp8_ds_profile_last reports, by their number.
+KERNEL_NAMES = {5: ("route", "permute", "gemm1", "gemm2", "finalize"), 3: ("route+permute", "gemm1", "gemm2+combine"),
+                1: ("fused_decode",)}
+
+
+def _gemm1_ms(m, T):
+    """GEMM1's event time of a call (0 when the call ran the fused decode kernel)."""
+    names = KERNEL_NAMES[m["nkern"][T]]
+    return float(m["kernel_ms"][T][names.index("gemm1")]) if "gemm1" in names else 0.0
+
+
 def _sweep_entry(wl, T, m, hbm_peak, fp8_nominal):
     st = m["stats"][T]
     ms = m["ms"][T]
@@ -395,8 +406,7 @@ def _sweep_entry(wl, T, m, hbm_peak, fp8_nominal):
         e["host_enqueue_us"] = round(m["host_us"][T], 1)
     if "kernel_ms" in m:
         k = m["kernel_ms"][T]
-        e["kernel_us"] = ({"fused_decode": round(k[0] * 1e3, 2)} if m["nkern"][T] == 1 else
-                          {n: round(v * 1e3, 2) for n, v in zip(("route", "gemm1", "gemm2"), k)})
+        e["kernel_us"] = {n: round(v * 1e3, 2) for n, v in zip(KERNEL_NAMES[m["nkern"][T]], k)}
     return e
 
 
@@ -407,8 +417,8 @@ def _run_sweep(pkg, lib, wl, dev, stream, flush, w32, name, steps, warmup, fp8, 
     hbm_peak, bf16_peak, peak_src = _peaks()
     m = _measure_layer(pkg, lib, dev, stream, flush, w32, acts, 32, steps, warmup)
     entries = {str(T): _sweep_entry(wl, T, m, hbm_peak, 2 * bf16_peak) for T in Ts}
-    g1_ms = sum(m["kernel_ms"][T][1] for T in Ts if m["nkern"][T] == 3)
-    roof = _roofline_gemm1([m["stats"][T] for T in Ts if m["nkern"][T] == 3], g1_ms, hbm_peak, peak_src, fp8,
+    g1_ms = sum(_gemm1_ms(m, T) for T in Ts if _gemm1_ms(m, T) > 0)
+    roof = _roofline_gemm1([m["stats"][T] for T in Ts if _gemm1_ms(m, T) > 0], g1_ms, hbm_peak, peak_src, fp8,
                            2 * _sustained_bf16(), f"gemm1_{name}")
     tot_ms = sum(m["ms"].values())
     return {"T": list(Ts), "us_mean": round(tot_ms * 1e3 / len(Ts), 3),
@@ -509,7 +519,7 @@ def bench_ep(args, rank, world, local, dev):
         ms = m["ms"][T]
         st = m["stats"][T]
         entry = _sweep_entry(wl, T, m, hbm_peak, 2 * bf16_peak)
-        roof = _roofline_gemm1([st], m["kernel_ms"][T][1], hbm_peak, peak_src, fp8, 2 * _sustained_bf16(),
+        roof = _roofline_gemm1([st], _gemm1_ms(m, T), hbm_peak, peak_src, fp8, 2 * _sustained_bf16(),
                                "gemm1_ep1")
         line.update({"value": round(ms * 1e3, 2), "ms_per_step": round(ms, 4), "tflops": entry["tflops"],
                      "detail": entry, "roofline": roof,

@@ -31,7 +31,7 @@ SIGNATURES = {
     "moe_fp8_ds_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "moe_fp8_ds_device_status": (ctypes.c_int, [_vp]),
     "moe_fp8_ds_workspace_bytes": (ctypes.c_size_t, [_c_int64, _c_int64]),
-    "moe_fp8_ds_last_rows": (ctypes.c_int, [_c_int64, _c_int64, _vp, _vp, _vp]),
+    "moe_fp8_ds_last_rows": (ctypes.c_int, [_c_int64, _c_int64, _vp, _vp]),
     "moe_fp8_ds_release_workspace": (ctypes.c_int, []),
     "moe_fp8_ds_version": (ctypes.c_char_p, []),
     "moe_fp8_ds_profile_enable": (ctypes.c_int, [ctypes.c_int]),

@@ -289,16 +289,15 @@ def add_rmsnorm_quantize(x: torch.Tensor, residual: torch.Tensor | None = None,
 
 def last_rows(seq_len: int, num_local_experts: int, device=None):
     """Where the last layer call with ``num_local_experts`` on ``device`` put
-    each token's expert rows: (local experts int32 [seq_len, 8] ascending, -1
-    padded; slots int32 [seq_len, 8]); slot s lies in the expert's m-tile
-    s // 128. A diagnostic for tests."""
+    each token's expert rows: int32 [seq_len, 8], the padded-layout row of the
+    token's j-th local expert (ascending id, -1 padded); row r lies in m-tile
+    r // 128, and each m-tile belongs to one expert. A diagnostic for tests."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    e = torch.empty((seq_len, TOP_K), dtype=torch.int32, device=dev)
-    sl = torch.empty((seq_len, TOP_K), dtype=torch.int32, device=dev)
-    rc = _call(dev, _lib.load().moe_fp8_ds_last_rows, int(seq_len), int(num_local_experts), e.data_ptr(),
-               sl.data_ptr(), _stream(dev))
+    rows = torch.empty((seq_len, TOP_K), dtype=torch.int32, device=dev)
+    rc = _call(dev, _lib.load().moe_fp8_ds_last_rows, int(seq_len), int(num_local_experts), rows.data_ptr(),
+               _stream(dev))
     _lib.check(rc, "moe_fp8_ds_last_rows")
-    return e, sl
+    return rows
 
 
 def device_status(stream=None) -> int:

@@ -1,6 +1,6 @@
 // moe_api.cu — the C ABI (include/moe_fp8_ds.h): argument checks, cached
 // device workspace, TMA tensor maps and the launch sequence
-//   route+plan -> GEMM1(gather + SwiGLU + requant) -> GEMM2(+weight + combine)
+//   route+plan -> permute -> GEMM1(+SwiGLU+requant) -> GEMM2(+combine) -> finalize
 // on the caller's stream, with no host synchronisation.
 #include <cstdlib>
 #include <mutex>
@@ -90,6 +90,7 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // (self-resetting counters, the combine accumulator, split-K scratch).
 size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_bytes, bool routing_only = false) {
   const int64_t rows = routing_only ? 0 : rows_cap_for(T, e_local);
+  const int ctas = route_ctas_for(static_cast<int>(T));
   size_t off = 0;
   auto take = [&](size_t bytes) {
     size_t o = off;
@@ -106,14 +107,15 @@ size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_
     w.topk_ids = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
     w.topk_w = reinterpret_cast<float*>(take(Tz * kTopK * 4));
     w.topk_rank = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
+    w.cta_off = reinterpret_cast<int32_t*>(take((size_t)(ctas > 256 ? ctas : 256) * kExperts * 4));
     w.rows_cap = 0;
     w.t_cap = T;
     w.e_local = e_local;
+    w.route_ctas_cap = ctas;
     return off;
   }
   w.tile_sem = reinterpret_cast<int32_t*>(take((size_t)kMaxSplitMTiles * kNT1 * 4));
   w.tile_sem2 = reinterpret_cast<int32_t*>(take((size_t)kMaxSplitMTiles * kNT2 * 4));
-  w.tok_cnt = reinterpret_cast<int32_t*>(take(Tz * kNT2 * 4 * 4));
   w.g_part = reinterpret_cast<float*>(take((size_t)kMaxSplitMTiles * kTileM * kGemm1N * 4));
   w.g2_part = reinterpret_cast<float*>(take((size_t)kMaxSplitMTiles * kTileM * kHidden * 4));
   // fused decode kernel scratch (independent of T)
@@ -131,21 +133,23 @@ size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_
   w.dec.inter = take((size_t)e_local * kDecMaxT * kInterCols);
   w.dec.inter_scale = reinterpret_cast<float*>(take((size_t)e_local * kInterBlocks * kDecMaxT * 4));
   w.dec.status = w.status;
+  w.token_rows = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
   w.out_rows = reinterpret_cast<__nv_bfloat16*>(take((size_t)rows * kHidden * 2));
   w.plan = reinterpret_cast<Plan*>(take(sizeof(Plan)));
   w.topk_ids = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
   w.topk_w = reinterpret_cast<float*>(take(Tz * kTopK * 4));
   w.topk_rank = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
-  w.etok = reinterpret_cast<int32_t*>(take((size_t)e_local * Tz * 4));
-  w.ew = reinterpret_cast<float*>(take((size_t)e_local * Tz * 4));
-  w.tok_e = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
-  w.tok_slot = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
-  w.tok_n = reinterpret_cast<int32_t*>(take(Tz * 4));
+  w.cta_off = reinterpret_cast<int32_t*>(take((size_t)(ctas > 256 ? ctas : 256) * e_local * 4));
+  w.a1 = take((size_t)rows * kHidden);
+  w.a1_scale = reinterpret_cast<float*>(take((size_t)rows * kHiddenBlocks * 4));
+  w.row_token = reinterpret_cast<int32_t*>(take((size_t)rows * 4));
+  w.row_weight = reinterpret_cast<float*>(take((size_t)rows * 4));
   w.inter = take((size_t)rows * kInterCols);
   w.inter_scale = reinterpret_cast<float*>(take((size_t)rows * kInterBlocks * 4));
   w.rows_cap = rows;
-  w.t_cap = static_cast<int64_t>(Tz);
+  w.t_cap = T;
   w.e_local = e_local;
+  w.route_ctas_cap = ctas;
   return off;
 }
 
@@ -206,9 +210,8 @@ int check_device() {
   return major_cache[dev] == 10 ? MOE_OK : MOE_ERR_NO_DEVICE;
 }
 
-// Optional per-kernel CUDA events (moe_fp8_ds_profile_enable): routing,
-// GEMM1, GEMM2.
-constexpr int kProfKernels = 3;
+// Optional per-kernel CUDA events (moe_fp8_ds_profile_enable).
+constexpr int kProfKernels = 5;
 bool g_prof_on = false;
 bool g_prof_valid = false;
 int g_prof_n = kProfKernels;  // intervals recorded by the last call (1 for the fused decode kernel)
@@ -306,30 +309,36 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
   ra.user_ids = user_ids;
   ra.user_w = user_w;
   ra.user_counts = user_counts;
-  ra.out = route_only ? nullptr : out;
-  ra.out_fp32 = out_fp32;
-  if (route_only) return launch_route(*ws, ra, s) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+  if (!route_only) prof_mark(0, s);
+  if (launch_route(*ws, ra, s) != cudaSuccess) return MOE_ERR_CUDA;
+  if (route_only) return MOE_OK;
 
   // calls with at most 64 rows use the skinny GEMM configuration (64-row
   // token tiles, one more stage of weights in flight)
   const bool skinny = T <= kSkinnyMaxRows;
   const uint32_t a_box = skinny ? kSkinnyMaxRows : kTileM;
-  // GEMM1 gathers token rows from hidden_states (one-row boxes, gather4)
-  CUtensorMap mx, mw1, ma2, mw2;
-  if (!make_map(&mx, hidden, kHidden, static_cast<uint64_t>(T), 1) ||
+  CUtensorMap ma1, mw1, ma2, mw2;
+  if (!make_map(&ma1, ws->a1, kHidden, ws->rows_cap, a_box) ||
       !make_map(&mw1, w1, kHidden, static_cast<uint64_t>(E_l) * kGemm1N) ||
       !make_map(&ma2, ws->inter, kInterCols, ws->rows_cap, a_box) ||
       !make_map(&mw2, w2, kInter, static_cast<uint64_t>(E_l) * kHidden))
     return MOE_ERR_CUDA;
 
-  prof_mark(0, s);
-  if (launch_route(*ws, ra, s) != cudaSuccess) return MOE_ERR_CUDA;
+  PermuteArgs pa{};
+  pa.hidden = static_cast<const uint8_t*>(hidden);
+  pa.hidden_scale = hidden_scale;
+  pa.T = static_cast<int>(T);
+  pa.offset = static_cast<int>(offset);
+  pa.tokens_per_cta = ra.tokens_per_cta;
   prof_mark(1, s);
-  if (launch_gemm1(*ws, mx, hidden_scale, static_cast<int>(T), mw1, s1, s, skinny) != cudaSuccess)
-    return MOE_ERR_CUDA;
+  if (launch_permute(*ws, pa, s) != cudaSuccess) return MOE_ERR_CUDA;
   prof_mark(2, s);
-  if (launch_gemm2(*ws, ma2, mw2, s2, out, out_fp32, s, skinny) != cudaSuccess) return MOE_ERR_CUDA;
+  if (launch_gemm1(*ws, ma1, mw1, s1, s, skinny) != cudaSuccess) return MOE_ERR_CUDA;
   prof_mark(3, s);
+  if (launch_gemm2(*ws, ma2, mw2, s2, s, skinny) != cudaSuccess) return MOE_ERR_CUDA;
+  prof_mark(4, s);
+  if (launch_finalize(*ws, static_cast<int>(T), out, out_fp32, s) != cudaSuccess) return MOE_ERR_CUDA;
+  prof_mark(5, s);
   g_prof_n = kProfKernels;
   g_prof_valid = g_prof_on;
   return MOE_OK;
@@ -509,10 +518,9 @@ int moe_fp8_ds_device_status(void* stream) {
   return rc;
 }
 
-int moe_fp8_ds_last_rows(int64_t seq_len, int64_t num_local_experts, int32_t* local_expert_out, int32_t* slot_out,
-                         void* stream) {
+int moe_fp8_ds_last_rows(int64_t seq_len, int64_t num_local_experts, int32_t* rows_out, void* stream) {
   if (seq_len < 0 || !valid_e_local(num_local_experts)) return MOE_ERR_INVALID_ARG;
-  if (seq_len > 0 && (!local_expert_out || !slot_out)) return MOE_ERR_INVALID_ARG;
+  if (seq_len > 0 && !rows_out) return MOE_ERR_INVALID_ARG;
   int rc = check_device();
   if (rc) return rc;
   if (seq_len == 0) return MOE_OK;
@@ -521,10 +529,8 @@ int moe_fp8_ds_last_rows(int64_t seq_len, int64_t num_local_experts, int32_t* lo
   std::lock_guard<std::mutex> lk(g_mu);
   auto it = g_ws.find(ws_key(dev, static_cast<int>(num_local_experts), false));
   if (it == g_ws.end() || !it->second.base || it->second.t_cap < seq_len) return MOE_ERR_INVALID_ARG;
-  const size_t bytes = static_cast<size_t>(seq_len) * kTopK * 4;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (cudaMemcpyAsync(local_expert_out, it->second.tok_e, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
-      cudaMemcpyAsync(slot_out, it->second.tok_slot, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+  if (cudaMemcpyAsync(rows_out, it->second.token_rows, static_cast<size_t>(seq_len) * kTopK * 4,
+                      cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return MOE_ERR_CUDA;
   return MOE_OK;
 }

@@ -1,34 +1,26 @@
 // moe_gemm.cu — K2/K3: persistent grouped block-scaled FP8 GEMMs on tcgen05.
 //
-//   GEMM1 (kMode = 1): G[r, :] = X[token(r), :] (e4m3, 1x128 scales) x W13[e]^T
+//   GEMM1 (kMode = 1): G[r, :] = A1[r, :] (e4m3, 1x128 scales) x W13[e]^T
 //     (e4m3, 128x128 scales), K = 7168, then SwiGLU (ref_moe.py:153-159:
 //     C = G[:, :2048] * silu(G[:, 2048:]), silu(x) = x / (1 + exp(-x))) and
 //     re-quantisation of C into a two-term e4m3 intermediate per 1x128 block:
 //     hi = e4m3(C / s), lo = e4m3(C / s - hi), s = amax / 448, so
-//     C ~= s * (hi + lo). The token rows are gathered straight from
-//     hidden_states (TMA tile::gather4, four rows per instruction) through the
-//     expert-major token lists the routing kernel wrote; no permuted copy of
-//     the activations exists.
+//     C ~= s * (hi + lo).
 //   GEMM2 (kMode = 2): O[r, :] = (hi + lo)[r, :] x W2[e]^T over 16 K blocks:
 //     per block the hi and lo tiles are both multiplied against the same W2
-//     tile into one TMEM partial (they share the scale s); the epilogue
-//     applies the routing weight and combines the expert rows of every token
-//     into the layer output (ref_moe.py:162-167): a token with one local
-//     expert is written directly; otherwise each expert row is stored in bf16
-//     and the last of the token's rows to arrive (per 64-column piece) sums
-//     them in fp32 in ascending expert id and casts once.
+//     tile into one TMEM partial (they share the scale s), then
+//     out_rows[r, :] = bf16(routing_weight(r) * O[r, :])  (ref_moe.py:162-166;
+//     the combine sums these rows in fp32).
 //
-// Warp roles (608 threads, one CTA per SM):
-//   warp 0      TMA producer: lane 0 waits for a free stage and loads the
-//               weight slabs (two 128x128 boxes per K block); GEMM1's token
-//               rows are gathered by lanes 0..31 (4 rows each), GEMM2's
-//               intermediate tiles by lane 0 (2D boxes).
+// Warp roles (576 threads, one CTA per SM):
+//   warp 0      TMA producer (one elected lane): A tile 128x128 + two B slabs
+//               128x128 per K block into a 4-stage shared-memory ring.
 //   warp 1      TMEM owner + MMA issuer (one lane): 4 x tcgen05.mma
 //               (M128 N256 K32, e4m3 x e4m3 -> f32) per K block into one of
 //               two 256-column TMEM partial accumulators.
-//   warp 2      scale loader: cp.async copies of the rows' activation scales
-//               and the weight-block scales of every K block into an 8-deep
-//               shared ring, running ahead of the epilogue.
+//   warp 2      scale loader: cp.async copies of the 128 row scales and the
+//               weight-block scales of every K block into an 8-deep shared
+//               ring, running ahead of the epilogue.
 //   warps 3-18  epilogue: per K block, read the fresh partial from TMEM and
 //               promote it in fp32 registers with a_scale[row,kb] *
 //               w_scale[nblk,kb] (the block scales are arbitrary fp32, so no
@@ -44,27 +36,18 @@ namespace {
 
 struct GemmArgs {
   const Plan* plan;
-  const float* a_scale;     // GEMM1: hidden_states_scale [56][T]; GEMM2: inter_scale [16][rows_cap]
-  int64_t a_scale_ld;       // row stride of a_scale: T (GEMM1) or rows_cap (GEMM2)
+  const float* a_scale;     // GEMM1: [56][rows_cap]; GEMM2: [16][rows_cap]
   const float* w_scale;     // GEMM1: [E_l][32][56];  GEMM2: [E_l][56][16]
   int rows_cap;
   int e_local;
-  int64_t t_cap;            // row stride of etok / ew
-  const int32_t* etok;      // [E_l][t_cap] token of each (expert, slot)
-  const float* ew;          // [E_l][t_cap] routing weight of each (expert, slot)
-  const int32_t* tok_e;     // [T][8] local experts of each token, ascending, -1 padded
-  const int32_t* tok_slot;  // [T][8] their slots
-  const int32_t* tok_n;     // [T] number of local experts of each token
-  int32_t* tok_cnt;         // [T][28][4] combine arrivals (kept zero)
   uint8_t* inter;           // GEMM1 out: [rows_cap][4096]
   float* inter_scale;       // GEMM1 out: [16][rows_cap]
   float* g_part;            // GEMM1 split-K scratch: [kMaxSplitMTiles*128][4096]
   int32_t* tile_sem;        // GEMM1 split-K counters: [kMaxSplitMTiles][16]
-  __nv_bfloat16* out_rows;  // GEMM2: [rows_cap][7168] weighted expert rows of multi-expert tokens (bf16)
+  const float* row_weight;  // GEMM2: routing weight of each permuted row
+  __nv_bfloat16* out_rows;  // GEMM2 out: [rows_cap][7168] weighted expert outputs (bf16)
   float* g2_part;           // GEMM2 split-K scratch: [kMaxSplitMTiles*128][7168]
   int32_t* tile_sem2;       // GEMM2 split-K counters: [kMaxSplitMTiles][28]
-  void* out;                // GEMM2: layer output [T][7168], bf16 or (out_fp32) f32
-  int out_fp32;
   unsigned* status;
   int plan_early;           // 1: the plan was complete before the previous kernel released this one
 };
@@ -156,6 +139,9 @@ __device__ __forceinline__ void promote16(float* acc, const float (&v)[16], floa
   }
 }
 
+// x * sigmoid(x) (ref_moe.py:157) with the fast exponential and reciprocal
+// intrinsics: relative error ~1e-7, far below the e4m3 requantisation that
+// follows, and a short code path (no division slow path).
 // 16 consecutive bf16 values w * v[0..15] (round to nearest even) as two uint4
 __device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, float w, const float* v) {
   uint32_t u[8];
@@ -169,106 +155,7 @@ __device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, float w, const
   d[1] = make_uint4(u[4], u[5], u[6], u[7]);
 }
 
-// 64 output columns [col0, col0 + 64) of token t. bf16 output: bf16(w * v).
-// f32 output: with `round`, the f32 value of bf16(w * v) (a single expert
-// row, as the combine would have read it back); without, w * v as is.
-__device__ __forceinline__ void store_out64(const GemmArgs& p, int t, int col0, const float* v, float w,
-                                            bool round) {
-  if (!p.out_fp32) {
-    __nv_bfloat16* d = static_cast<__nv_bfloat16*>(p.out) + (size_t)t * kHidden + col0;
-#pragma unroll
-    for (int i = 0; i < 64; i += 16) store_bf16x16(d + i, w, v + i);
-  } else {
-    float4* d = reinterpret_cast<float4*>(static_cast<float*>(p.out) + (size_t)t * kHidden + col0);
-#pragma unroll
-    for (int i = 0; i < 64; i += 4) {
-      float4 q = make_float4(w * v[i], w * v[i + 1], w * v[i + 2], w * v[i + 3]);
-      if (round) {
-        q.x = __bfloat162float(__float2bfloat16_rn(q.x));
-        q.y = __bfloat162float(__float2bfloat16_rn(q.y));
-        q.z = __bfloat162float(__float2bfloat16_rn(q.z));
-        q.w = __bfloat162float(__float2bfloat16_rn(q.w));
-      }
-      d[i / 4] = q;
-    }
-  }
-}
-
-// Combine (ref_moe.py:134-167) of 64 columns of one expert row: slot `row` of
-// the padded layout, token t, GEMM2 n-tile n, column group cg, unweighted
-// result v (routing weight w). A token with one local expert is written to the
-// output directly. Otherwise the row is stored as a bf16 expert row, and the
-// last of the token's rows to arrive for these 64 columns sums all of them in
-// fp32 in ascending expert id and writes the output, as the reference's fp32
-// index_add in expert order followed by one bf16 cast does. The arrival
-// counter is left at zero for the next call.
-__device__ __forceinline__ void combine64(const GemmArgs& p, const int* prefix, int t, size_t row, int n, int cg,
-                                          float* v, float w) {
-  const int col0 = n * kTileN + cg * 64;
-  const int nloc = __ldg(p.tok_n + t);
-  if (nloc == 1) {
-    store_out64(p, t, col0, v, w, true);
-    return;
-  }
-  __nv_bfloat16* dst = p.out_rows + row * kHidden + col0;
-#pragma unroll
-  for (int i = 0; i < 64; i += 16) store_bf16x16(dst + i, w, v + i);
-  __threadfence();
-  int* cnt = p.tok_cnt + ((size_t)t * kNT2 + n) * 4 + cg;
-  if (atomicAdd(cnt, 1) != nloc - 1) return;
-  __threadfence();
-  *cnt = 0;
-#pragma unroll
-  for (int i = 0; i < 64; ++i) v[i] = 0.f;
-  for (int j = 0; j < nloc; ++j) {
-    const int e = __ldg(p.tok_e + (size_t)t * kTopK + j);
-    const int sl = __ldg(p.tok_slot + (size_t)t * kTopK + j);
-    const uint4* src =
-        reinterpret_cast<const uint4*>(p.out_rows + ((size_t)prefix[e] * kTileM + sl) * kHidden + col0);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      // 8 bf16 columns; bf16 -> f32 is exact (upper half of the word)
-      const uint4 b = __ldcg(src + q);
-      float* a = v + 8 * q;
-      a[0] += __uint_as_float(b.x << 16); a[1] += __uint_as_float(b.x & 0xFFFF0000u);
-      a[2] += __uint_as_float(b.y << 16); a[3] += __uint_as_float(b.y & 0xFFFF0000u);
-      a[4] += __uint_as_float(b.z << 16); a[5] += __uint_as_float(b.z & 0xFFFF0000u);
-      a[6] += __uint_as_float(b.w << 16); a[7] += __uint_as_float(b.w & 0xFFFF0000u);
-    }
-  }
-  store_out64(p, t, col0, v, 1.0f, false);
-}
-
-// x * sigmoid(x) (ref_moe.py:157) with the fast exponential and reciprocal
-// intrinsics: relative error ~1e-7, far below the e4m3 requantisation that
-// follows, and a short code path (no division slow path).
 __device__ __forceinline__ float silu_ref(float x) { return x * __frcp_rn(1.0f + __expf(-x)); }
-
-// Bytes one pipeline stage receives: the two weight slabs plus, for GEMM1,
-// the gathered token rows (groups of four; the last group repeats the unit's
-// last row) or, for GEMM2, the hi and lo intermediate boxes.
-template <int kMode, int kSkinny>
-__device__ __forceinline__ uint32_t stage_tx_bytes(int rows) {
-  using Cfg = GemmCfg<kMode, kSkinny>;
-  if (kMode == 1) return static_cast<uint32_t>(kStageB + ((rows + 3) >> 2) * 4 * kBlk);
-  return static_cast<uint32_t>(Cfg::kStageBytes);
-}
-
-// The weight slabs of K block kb of unit x: GEMM1 128 gate rows + the matching
-// 128 up rows of W13[e]; GEMM2 256 rows of W2[e].
-template <int kMode>
-__device__ __forceinline__ void load_weights(uint8_t* sb, const CUtensorMap* map_w, const Unit& x, int kb,
-                                             uint64_t* bar) {
-  if (kMode == 1) {
-    const int y0 = x.e * kGemm1N + x.n * kBlk;
-    tma_load_2d(sb, map_w, kb * kBlk, y0, bar);
-    tma_load_2d(sb + kStageA, map_w, kb * kBlk, y0 + kInter, bar);
-  } else {
-    const int y0 = x.e * kHidden + x.n * kTileN;
-    tma_load_2d(sb, map_w, kb * kBlk, y0, bar);
-    tma_load_2d(sb + kStageA, map_w, kb * kBlk, y0 + kBlk, bar);
-  }
-}
 
 __device__ __forceinline__ float e4m3_byte_to_f32(uint32_t b) {
   uint32_t h2;
@@ -396,8 +283,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const Unit x = decode_unit<kMode>(u, split0, ctl->prefix, ctl->count, E_l);
       for (int kb = x.kb0; kb < x.kb1 && n_pre < kStages; ++kb, ++n_pre) {
         uint8_t* sb = tiles + n_pre * kStageBytes + kBOff;
-        mbar_arrive_expect_tx(&ctl->full[n_pre], stage_tx_bytes<kMode, kSkinny>(x.rows));
-        load_weights<kMode>(sb, &map_w, x, kb, &ctl->full[n_pre]);
+        mbar_arrive_expect_tx(&ctl->full[n_pre], kStageBytes);
+        if (kMode == 1) {
+          const int y0 = x.e * kGemm1N + x.n * kBlk;
+          tma_load_2d(sb, &map_w, kb * kBlk, y0, &ctl->full[n_pre]);
+          tma_load_2d(sb + kStageA, &map_w, kb * kBlk, y0 + kInter, &ctl->full[n_pre]);
+        } else {
+          const int y0 = x.e * kHidden + x.n * kTileN;
+          tma_load_2d(sb, &map_w, kb * kBlk, y0, &ctl->full[n_pre]);
+          tma_load_2d(sb + kStageA, &map_w, kb * kBlk, y0 + kBlk, &ctl->full[n_pre]);
+        }
       }
     }
   }
@@ -416,49 +311,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (warp == 0) {
     // ======================= TMA producer =======================
-    uint32_t it = 0;
-    bool ok = true;
-    for (int u = blockIdx.x; u < units; u += gridDim.x) {
-      if (__shfl_sync(0xffffffffu, aborted(ctl) ? 1 : 0, 0)) break;
-      const Unit x = decode_unit<kMode>(u, split, ctl->prefix, ctl->count, E_l);
-      // GEMM1: lane l gathers rows 4l..4l+3 of the unit (groups past the last
-      // row are not loaded; the last group repeats the last row)
-      const int ngroups = (x.rows + 3) >> 2;
-      int y[4] = {0, 0, 0, 0};
-      if (kMode == 1 && lane < ngroups) {
-        const int32_t* et = p.etok + (size_t)x.e * p.t_cap + (size_t)x.m * kTileM;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) y[i] = __ldg(et + min(4 * lane + i, x.rows - 1));
-      }
-      for (int kb = x.kb0; kb < x.kb1; ++kb, ++it) {
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1u;
-        uint8_t* sa = tiles + s * kStageBytes;
-        if (lane == 0 && static_cast<int>(it) >= n_pre) {
-          ok = mbar_wait_bounded(&ctl->empty[s], ph ^ 1u, kWaitLimitNs);
-          if (ok) {
-            mbar_arrive_expect_tx(&ctl->full[s], stage_tx_bytes<kMode, kSkinny>(x.rows));
-            load_weights<kMode>(sa + kBOff, &map_w, x, kb, &ctl->full[s]);
-          }
-        }
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        if (!ok) break;
-        // token rows; the weights of a prefetched stage are already in flight
-        if (kMode == 1) {
-          if (lane < ngroups)
-            tma_gather4(sa + lane * 4 * kBlk, &map_a, kb * kBlk, y[0], y[1], y[2], y[3], &ctl->full[s]);
-        } else if (lane == 0) {
-          tma_load_2d(sa, &map_a, kb * kBlk, x.gm * kTileM, &ctl->full[s]);
-          tma_load_2d(sa + kABytes, &map_a, kInter + kb * kBlk, x.gm * kTileM, &ctl->full[s]);
-        }
-      }
-      if (!ok) break;
-    }
     if (lane == 0) {
-      if (!ok) signal_abort(ctl, p.status);
+      uint32_t it = 0;
+      for (int u = blockIdx.x; u < units && !aborted(ctl); u += gridDim.x) {
+        const Unit x = decode_unit<kMode>(u, split, ctl->prefix, ctl->count, E_l);
+        for (int kb = x.kb0; kb < x.kb1; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1u;
+          uint8_t* sa = tiles + s * kStageBytes;
+          uint8_t* sb = sa + kBOff;
+          if (static_cast<int>(it) >= n_pre) {
+            if (!mbar_wait_bounded(&ctl->empty[s], ph ^ 1u, kWaitLimitNs)) { signal_abort(ctl, p.status); break; }
+            mbar_arrive_expect_tx(&ctl->full[s], kStageBytes);
+            if (kMode == 1) {
+              const int y0 = x.e * kGemm1N + x.n * kBlk;
+              tma_load_2d(sb, &map_w, kb * kBlk, y0, &ctl->full[s]);
+              tma_load_2d(sb + kStageA, &map_w, kb * kBlk, y0 + kInter, &ctl->full[s]);
+            } else {
+              const int y0 = x.e * kHidden + x.n * kTileN;
+              tma_load_2d(sb, &map_w, kb * kBlk, y0, &ctl->full[s]);
+              tma_load_2d(sb + kStageA, &map_w, kb * kBlk, y0 + kBlk, &ctl->full[s]);
+            }
+          }
+          // token tile(s); the weights of a prefetched stage are already in flight
+          tma_load_2d(sa, &map_a, kb * kBlk, x.gm * kTileM, &ctl->full[s]);
+          if (kMode == 2) tma_load_2d(sa + kABytes, &map_a, kInter + kb * kBlk, x.gm * kTileM, &ctl->full[s]);
+        }
+        if (aborted(ctl)) break;
+      }
       if (aborted(ctl)) {
-        // drain: wait (bounded) for the loads this warp may still have in flight
-        const uint32_t n_issued = it > static_cast<uint32_t>(n_pre) ? it : static_cast<uint32_t>(n_pre);
+        // drain: wait (bounded) for the loads this thread may still have in flight
+        const uint32_t n_issued = it;
         for (uint32_t j = (n_issued > (uint32_t)kStages ? n_issued - kStages : 0); j < n_issued; ++j)
           mbar_wait_bounded(&ctl->full[j % kStages], (j / kStages) & 1u, kWaitLimitNs);
       }
@@ -509,17 +392,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == kScaleWarp) {
     // ======================= scale loader =======================
     uint32_t it = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x) {
-      if (__shfl_sync(0xffffffffu, aborted(ctl) ? 1 : 0, 0)) break;
+    for (int u = blockIdx.x; u < units && !aborted(ctl); u += gridDim.x) {
       const Unit x = decode_unit<kMode>(u, split, ctl->prefix, ctl->count, E_l);
-      // GEMM1: the tokens of rows 4l..4l+3 (-1 past the unit's last row)
-      int y[4] = {-1, -1, -1, -1};
-      if (kMode == 1) {
-        const int32_t* et = p.etok + (size_t)x.e * p.t_cap + (size_t)x.m * kTileM;
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          if (4 * lane + i < x.rows) y[i] = __ldg(et + 4 * lane + i);
-      }
       bool ok = true;
       for (int kb = x.kb0; kb < x.kb1; ++kb, ++it) {
         const int j = it % kScaleSlots;
@@ -530,20 +404,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         ScaleSlot* sl = &ctl->scales[j];
-        if (kMode == 1) {
-          // hidden_states_scale [56][T]: block kb of each gathered token
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            if (y[i] >= 0) cp_async_4(&sl->a[4 * lane + i], p.a_scale + (size_t)kb * p.a_scale_ld + y[i]);
-        } else {
-          cp_async_16(&sl->a[4 * lane], p.a_scale + (size_t)kb * p.a_scale_ld + (size_t)x.gm * kTileM + 4 * lane);
-        }
+        const int ka = kb;
+        cp_async_16(&sl->a[4 * lane], p.a_scale + (size_t)ka * p.rows_cap + (size_t)x.gm * kTileM + 4 * lane);
         if (lane < 2) {
           const float* src;
           if (kMode == 1)
             src = p.w_scale + ((size_t)x.e * kGemm1NBlocks + lane * kNT1 + x.n) * kHiddenBlocks + kb;
           else
-            src = p.w_scale + ((size_t)x.e * kHiddenBlocks + 2 * x.n + lane) * kInterBlocks + kb;
+            src = p.w_scale + ((size_t)x.e * kHiddenBlocks + 2 * x.n + lane) * kInterBlocks + ka;
           cp_async_4(&sl->w[lane], src);
         }
         cp_async_arrive_noinc(&ctl->sfull[j]);
@@ -662,19 +530,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if (do_swiglu) swiglu_quant_store(acc, acc + 32, cg, row_in_tile, valid, row, x.n, ctl, p, es);
       } else {
-        // routing weight and token of this row (slot m*128 + row of expert e)
-        const size_t slot = (size_t)x.m * kTileM + row_in_tile;
-        int t = 0;
-        float w = 0.f;
-        if (valid) {
-          t = __ldg(p.etok + (size_t)x.e * p.t_cap + slot);
-          w = __ldg(p.ew + (size_t)x.e * p.t_cap + slot);
-        }
+        const float w = valid ? __ldg(p.row_weight + row) : 0.f;
+        __nv_bfloat16* dst = p.out_rows + row * kHidden + x.n * kTileN + cg * 64;
         if (split == 1) {
-          if (valid) combine64(p, ctl->prefix, t, row, x.n, cg, acc, w);
+          if (valid) {
+#pragma unroll
+            for (int i = 0; i < 64; i += 16) store_bf16x16(dst + i, w, acc + i);
+          }
         } else {
           // split-K: partial sums meet in fp32 scratch; the last arriving CTA
-          // of this (m-tile, n-tile) combines the finished rows.
+          // of this (m-tile, n-tile) writes the finished rows.
           float* g = p.g2_part + row * kHidden + x.n * kTileN + cg * 64;
           if (valid) {
 #pragma unroll
@@ -691,7 +556,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (ctl->fixup_flag) {
             __threadfence();
             if (valid) {
-              // all loads first (independent), then clear the scratch
+              // all loads first (independent), then the stores
               float4* pg = reinterpret_cast<float4*>(g);
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
@@ -700,7 +565,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               }
 #pragma unroll
               for (int i = 0; i < 16; ++i) __stcg(pg + i, make_float4(0.f, 0.f, 0.f, 0.f));
-              combine64(p, ctl->prefix, t, row, x.n, cg, acc, 1.0f);
+#pragma unroll
+              for (int i = 0; i < 64; i += 16) store_bf16x16(dst + i, 1.0f, acc + i);
             }
             if (warp == kEpiWarp0 && lane == 0) p.tile_sem2[x.gm * kNT2 + x.n] = 0;
           }
@@ -722,8 +588,7 @@ size_t gemm_smem_bytes() { return kRingBytes + sizeof(SmemCtl) + 1024; }
 
 template <int kMode, int kSkinny>
 cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
-                        const float* a_scale, int64_t a_scale_ld, const float* w_scale, void* out, int out_fp32,
-                        cudaStream_t s, int plan_early) {
+                        const float* w_scale, cudaStream_t s, int plan_early) {
   // The shared-memory opt-in is a per-device function attribute: one bit per
   // device that has it (launches run under the library's host mutex).
   static uint64_t configured = 0;
@@ -741,27 +606,18 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
   const int sms = device_sm_count();
   GemmArgs p{};
   p.plan = ws.plan;
-  p.a_scale = a_scale;
-  p.a_scale_ld = a_scale_ld;
+  p.a_scale = (kMode == 1) ? ws.a1_scale : ws.inter_scale;
   p.w_scale = w_scale;
   p.rows_cap = static_cast<int>(ws.rows_cap);
   p.e_local = ws.e_local;
-  p.t_cap = ws.t_cap;
-  p.etok = ws.etok;
-  p.ew = ws.ew;
-  p.tok_e = ws.tok_e;
-  p.tok_slot = ws.tok_slot;
-  p.tok_n = ws.tok_n;
-  p.tok_cnt = ws.tok_cnt;
   p.inter = ws.inter;
   p.inter_scale = ws.inter_scale;
   p.g_part = ws.g_part;
   p.tile_sem = ws.tile_sem;
+  p.row_weight = ws.row_weight;
   p.out_rows = ws.out_rows;
   p.g2_part = ws.g2_part;
   p.tile_sem2 = ws.tile_sem2;
-  p.out = out;
-  p.out_fp32 = out_fp32;
   p.status = ws.status;
   p.plan_early = plan_early;
   return launch_k(moe_gemm_kernel<kMode, kSkinny>, dim3(sms), dim3(kGemmThreads), smem, s, true, map_a, map_w, p);
@@ -769,20 +625,18 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
 
 }  // namespace
 
-// GEMM1 directly follows the routing kernel, so it reads the plan only after
-// its programmatic-launch wait. GEMM2 follows GEMM1, which released it after
-// its own wait on the routing kernel: the plan is complete before GEMM2
-// starts, and GEMM2 loads it and issues its first weight tiles before waiting.
-cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_x, const float* x_scale, int T,
-                         const CUtensorMap& map_w, const float* w_scale, cudaStream_t s, bool skinny) {
-  return skinny ? launch_gemm<1, 1>(ws, map_x, map_w, x_scale, T, w_scale, nullptr, 0, s, 0)
-                : launch_gemm<1, 0>(ws, map_x, map_w, x_scale, T, w_scale, nullptr, 0, s, 0);
+// The permutation kernel runs between the routing kernel and GEMM1, so both
+// GEMMs may read the plan before their programmatic-launch wait.
+cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
+                         const float* w_scale, cudaStream_t s, bool skinny) {
+  return skinny ? launch_gemm<1, 1>(ws, map_a, map_w, w_scale, s, 1)
+                : launch_gemm<1, 0>(ws, map_a, map_w, w_scale, s, 1);
 }
 
 cudaError_t launch_gemm2(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
-                         const float* w_scale, void* out, int out_fp32, cudaStream_t s, bool skinny) {
-  return skinny ? launch_gemm<2, 1>(ws, map_a, map_w, ws.inter_scale, ws.rows_cap, w_scale, out, out_fp32, s, 1)
-                : launch_gemm<2, 0>(ws, map_a, map_w, ws.inter_scale, ws.rows_cap, w_scale, out, out_fp32, s, 1);
+                         const float* w_scale, cudaStream_t s, bool skinny) {
+  return skinny ? launch_gemm<2, 1>(ws, map_a, map_w, w_scale, s, 1)
+                : launch_gemm<2, 0>(ws, map_a, map_w, w_scale, s, 1);
 }
 
 }  // namespace moe

@@ -49,33 +49,27 @@ struct Workspace {
   int64_t t_cap = 0;       // tokens (rows of the caller's tensors) it was sized for
   int e_local = 0;         // local experts it was sized for
   int64_t rows_cap = 0;    // rows of the expert-major padded layout
+  int route_ctas_cap = 0;  // routing CTAs it was sized for
 
   int32_t* topk_ids = nullptr;     // [t_cap][8] global expert ids
   float* topk_w = nullptr;         // [t_cap][8]
   int32_t* topk_rank = nullptr;    // [t_cap][8] rank inside (routing CTA, expert), -1 = not local
+  int32_t* cta_off = nullptr;      // [route_ctas_cap][e_local] first slot of each CTA in an expert
   int32_t* expert_fill = nullptr;  // [e_local] running counters (self-resetting)
   uint32_t* done_ctas = nullptr;   // routing CTAs finished (self-resetting)
   Plan* plan = nullptr;
-  // Expert-major token lists written by the routing kernel. Slot s of local
-  // expert e is row (plan.mtile_prefix[e] * 128 + s) of the padded layout that
-  // the intermediate and the expert output rows use; the token rows themselves
-  // are gathered by GEMM1 straight from hidden_states.
-  int32_t* etok = nullptr;         // [e_local][t_cap] token of each slot
-  float* ew = nullptr;             // [e_local][t_cap] routing weight of each slot
-  // Per token: its local (expert, slot) pairs in ascending expert id (the
-  // order in which ref_moe.py:134-166 accumulates), -1 padded, and their count.
-  int32_t* tok_e = nullptr;        // [t_cap][8] local expert
-  int32_t* tok_slot = nullptr;     // [t_cap][8] slot inside that expert
-  int32_t* tok_n = nullptr;        // [t_cap]
-  int32_t* tok_cnt = nullptr;      // [t_cap][28][4] GEMM2 arrivals per (token, 64-column piece) (kept zero)
+  uint8_t* a1 = nullptr;           // [rows_cap][7168] permuted e4m3 token rows
+  float* a1_scale = nullptr;       // [56][rows_cap]
+  int32_t* row_token = nullptr;    // [rows_cap] source token of each permuted row
+  float* row_weight = nullptr;     // [rows_cap] routing weight of each permuted row
   uint8_t* inter = nullptr;        // [rows_cap][4096] two-term e4m3 intermediate (hi | lo)
   float* inter_scale = nullptr;    // [16][rows_cap] hi scales (lo = hi / 16)
   float* g_part = nullptr;         // [kMaxSplitMTiles*128][4096] GEMM1 split-K partial sums (kept zero)
   int32_t* tile_sem = nullptr;     // [kMaxSplitMTiles][16] GEMM1 split-K arrival counters (kept zero)
   float* g2_part = nullptr;        // [kMaxSplitMTiles*128][7168] GEMM2 split-K partial sums (kept zero)
   int32_t* tile_sem2 = nullptr;    // [kMaxSplitMTiles][28] GEMM2 split-K arrival counters (kept zero)
-  __nv_bfloat16* out_rows = nullptr;  // [rows_cap][7168] routing-weighted expert rows of tokens with more than
-                                      // one local expert (bf16), read back by the combine
+  __nv_bfloat16* out_rows = nullptr;  // [rows_cap][7168] routing-weighted expert output of every permuted row (bf16)
+  int32_t* token_rows = nullptr;   // [t_cap][8] permuted rows of each token, ascending expert id, -1 padded
   unsigned* status = nullptr;      // device status word (kErrTimeout ...)
   DecodeBuffers dec;               // scratch of the fused decode kernel
   void* base = nullptr;            // single allocation backing everything above
@@ -96,10 +90,14 @@ struct RouteArgs {
   int32_t* user_ids;          // optional outputs
   float* user_w;
   int32_t* user_counts;
-  // Full pipeline only (nullptr for routing alone): the layer output, whose
-  // rows of tokens without a local expert the routing kernel zeroes.
-  void* out;
-  int out_fp32;
+};
+
+struct PermuteArgs {
+  const uint8_t* hidden;      // [T][7168]
+  const float* hidden_scale;  // [56][T]
+  int T;
+  int offset;
+  int tokens_per_cta;
 };
 
 // Launch `kernel` on `s`; with `pdl` the launch may overlap the tail of the
@@ -129,16 +127,14 @@ int device_sm_count();  // cached per device
 int tokens_per_cta_for(int T, int ctas_per_sm = kRouteCtasPerSm);
 
 cudaError_t launch_route(const Workspace& ws, const RouteArgs& a, cudaStream_t s);
-// GEMM1 gathers its token rows from hidden_states: map_x is hidden_states
-// [T][7168] with one-row boxes (tile::gather4), x_scale its [56][T] scales.
-// skinny: every m-tile has at most kSkinnyMaxRows valid rows.
-cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_x, const float* x_scale, int T,
-                         const CUtensorMap& map_w, const float* w_scale, cudaStream_t s, bool skinny);
-// GEMM2 reads the intermediate through map_a (kSkinnyMaxRows- or 128-row
-// boxes) and writes the layer output `out` [T][7168] (bf16, or f32 with
-// out_fp32) for every token with a local expert.
+cudaError_t launch_permute(const Workspace& ws, const PermuteArgs& a, cudaStream_t s);
+// skinny: every m-tile has at most kSkinnyMaxRows valid rows (map_a then has
+// kSkinnyMaxRows-row boxes)
+cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
+                         const float* w_scale, cudaStream_t s, bool skinny);
 cudaError_t launch_gemm2(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
-                         const float* w_scale, void* out, int out_fp32, cudaStream_t s, bool skinny);
+                         const float* w_scale, cudaStream_t s, bool skinny);
+cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32, cudaStream_t s);
 
 // Expert-parallel token exchange (packed 7456-byte rows, see moe_ep.cu)
 cudaError_t launch_ep_pack(const void* hidden, const float* hidden_scale, const int32_t* ids, const float* w, int T,

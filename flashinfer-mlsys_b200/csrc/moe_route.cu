@@ -1,6 +1,6 @@
-// moe_route.cu — K1: DeepSeek-V3 no-aux routing + local histogram + the
-// expert-major token lists and the device-side tile plan that both GEMMs
-// read (no host synchronisation).
+// moe_route.cu — K1 (DeepSeek-V3 no-aux routing + local histogram + plan),
+// K1b (token permutation into the expert-major padded layout) and K4
+// (fp32 combine accumulator -> bf16/fp32 output).
 //
 // Routing semantics follow reference moe/ref_moe.py:95-126:
 //   s = 1 / (1 + exp(-logit)); sb = s + bias
@@ -25,59 +25,74 @@ constexpr int kMinTokensPerCta = 8;
 #endif
 constexpr int kSplitUnitOverhead = MOE_SPLIT_UNIT_OVERHEAD;
 
-// One warp, one token, after its routing CTA knows its base slot inside every
-// expert (`s_off`): record the token in the expert-major lists GEMM1 gathers
-// from (etok/ew, slot = base + rank inside the CTA), its local (expert, slot)
-// pairs in ascending expert id (the order in which ref_moe.py:134-166
-// accumulates the experts, -1 padded) and their number; a token with no local
-// expert gets its output row zeroed here (kernel.cu:206-209: every element of
-// the DPS output is written).
-__device__ __forceinline__ void scatter_token(int t, int lane, const RouteArgs& a, const int* s_off,
-                                              const Workspace& ws) {
-  int le = -1, slot = -1;
+// One warp, one token: copy the e4m3 row (7168 B) and its 56 block scales to
+// every local expert slot the token was routed to, and record the token's
+// rows. `prefix` is the m-tile prefix of the local experts.
+__device__ __forceinline__ void permute_token(int t, int lane, const uint8_t* __restrict__ hidden,
+                                              const float* __restrict__ hidden_scale, int T, int offset,
+                                              int tokens_per_cta, const int* prefix, const Workspace& ws) {
+  const int E_l = ws.e_local;
+  int row = -1;
+  float w = 0.f;
   if (lane < kTopK) {
     const size_t o = (size_t)t * kTopK + lane;
     const int r = ws.topk_rank[o];
     if (r >= 0) {
-      le = ws.topk_ids[o] - a.offset;
-      slot = s_off[le] + r;
-      ws.etok[(size_t)le * ws.t_cap + slot] = t;
-      ws.ew[(size_t)le * ws.t_cap + slot] = ws.topk_w[o];
+      const int le = ws.topk_ids[o] - offset;
+      const int cta = t / tokens_per_cta;
+      row = prefix[le] * kTileM + ws.cta_off[(size_t)cta * E_l + le] + r;
+      w = ws.topk_w[o];
     }
   }
-  // a token's experts are distinct, so the rank among its local ones is unique
-  const int key = le >= 0 ? le : 0x7fffffff;
-  int rank = 0;
+  // token_rows[t]: this token's rows in ascending expert id (the order in which
+  // ref_moe.py:134-166 accumulates the experts), -1 padded
+  {
+    const int my_e = (row >= 0) ? ws.topk_ids[(size_t)t * kTopK + lane] : 0x7fffffff;
+    int rank = 0, n_loc = 0;
 #pragma unroll
-  for (int k = 0; k < kTopK; ++k) rank += (__shfl_sync(0xffffffffu, key, k) < key) ? 1 : 0;
-  const int n_loc = __popc(__ballot_sync(0xffffffffu, le >= 0));
-  if (lane < kTopK) {
-    if (le >= 0) {
-      ws.tok_e[(size_t)t * kTopK + rank] = le;
-      ws.tok_slot[(size_t)t * kTopK + rank] = slot;
+    for (int k = 0; k < kTopK; ++k) {
+      const int ek = __shfl_sync(0xffffffffu, my_e, k);
+      const int rk = __shfl_sync(0xffffffffu, row, k);
+      rank += (rk >= 0 && (ek < my_e || (ek == my_e && k < lane))) ? 1 : 0;
+      n_loc += (rk >= 0) ? 1 : 0;
     }
-    if (lane >= n_loc) {
-      ws.tok_e[(size_t)t * kTopK + lane] = -1;
-      ws.tok_slot[(size_t)t * kTopK + lane] = -1;
+    if (lane < kTopK) {
+      if (row >= 0) ws.token_rows[(size_t)t * kTopK + rank] = row;
+      if (lane >= n_loc) ws.token_rows[(size_t)t * kTopK + lane] = -1;
     }
   }
-  if (lane == 0) ws.tok_n[t] = n_loc;
-  if (n_loc == 0) {
-    const int n16 = a.out_fp32 ? kHidden * 4 / 16 : kHidden * 2 / 16;
-    uint4* o = reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.out) + (size_t)t * (n16 * 16));
-    for (int i = lane; i < n16; i += 32) o[i] = make_uint4(0u, 0u, 0u, 0u);
+  const unsigned has = __ballot_sync(0xffffffffu, row >= 0);
+  if (!has) return;
+  const uint4* src = reinterpret_cast<const uint4*>(hidden + (size_t)t * kHidden);
+  const float sc0 = __ldg(hidden_scale + (size_t)lane * T + t);
+  const float sc1 = (lane + 32 < kHiddenBlocks) ? __ldg(hidden_scale + (size_t)(lane + 32) * T + t) : 0.f;
+  unsigned m = has;
+  while (m) {
+    const int k = __ffs(m) - 1;
+    m &= m - 1;
+    const int r = __shfl_sync(0xffffffffu, row, k);
+    const float wk = __shfl_sync(0xffffffffu, w, k);
+    // 14 chunks of 16 B per lane; repeated destinations re-read the row from L1
+    uint4* dst = reinterpret_cast<uint4*>(ws.a1 + (size_t)r * kHidden);
+#pragma unroll 7
+    for (int i = 0; i < kHidden / 16 / 32; ++i) dst[lane + 32 * i] = __ldg(src + lane + 32 * i);
+    ws.a1_scale[(size_t)lane * ws.rows_cap + r] = sc0;
+    if (lane + 32 < kHiddenBlocks) ws.a1_scale[(size_t)(lane + 32) * ws.rows_cap + r] = sc1;
+    if (lane == 0) {
+      ws.row_token[r] = t;
+      ws.row_weight[r] = wk;
+    }
   }
 }
 
 __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, Workspace ws) {
   __shared__ int hist[kExperts];
-  __shared__ int s_off[kExperts];  // this CTA's first slot inside every expert
   __shared__ int is_last;
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int E_l = a.e_local;
-  // first kernel of a call: launched with normal stream ordering; let GEMM1
-  // get scheduled early (it runs its prologue, then waits for this grid).
+  // first kernel of a call: launched with normal stream ordering; let the
+  // permutation kernel get scheduled early (it waits for this grid).
   griddep_launch_dependents();
   for (int e = tid; e < E_l; e += blockDim.x) hist[e] = 0;
   __syncthreads();
@@ -108,22 +123,19 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
   }
   __syncthreads();
 
-  // ---- this CTA's base slot inside every expert ----
-  const bool single = gridDim.x == 1;
-  for (int e = tid; e < E_l; e += blockDim.x) {
-    const int h = hist[e];
-    s_off[e] = (single || !h) ? 0 : atomicAdd(&ws.expert_fill[e], h);
-  }
-  __syncthreads();
-  // ---- expert-major token lists and per-token slots (full pipeline only) ----
-  if (ws.etok != nullptr) {
-    for (int t = t_begin + warp; t < t_end; t += nwarps) scatter_token(t, lane, a, s_off, ws);
-  }
   int c = 0;
-  if (single) {
+  if (gridDim.x == 1) {
     // single CTA: the shared histogram is the whole story
-    if (tid < E_l) c = hist[tid];
+    if (tid < E_l) {
+      c = hist[tid];
+      ws.cta_off[tid] = 0;
+    }
   } else {
+    // ---- publish this CTA's histogram: its base slot inside every expert ----
+    for (int e = tid; e < E_l; e += blockDim.x) {
+      const int h = hist[e];
+      ws.cta_off[(size_t)blockIdx.x * E_l + e] = h ? atomicAdd(&ws.expert_fill[e], h) : 0;
+    }
     __threadfence();
     __syncthreads();
     if (tid == 0) is_last = (atomicAdd(ws.done_ctas, 1u) == gridDim.x - 1) ? 1 : 0;
@@ -189,6 +201,60 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
   }
 }
 
+__global__ void __launch_bounds__(256) permute_kernel(PermuteArgs a, Workspace ws) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  griddep_wait();
+  griddep_launch_dependents();
+  if (t >= a.T) return;
+  permute_token(t, lane, a.hidden, a.hidden_scale, a.T, a.offset, a.tokens_per_cta, ws.plan->mtile_prefix, ws);
+}
+
+// out[t, :] = sum over the token's local rows (ascending expert id) of the
+// routing-weighted expert outputs (bf16 rows written by GEMM2), in fp32, then
+// cast once (ref_moe.py:166-167). Eight columns per thread.
+__global__ void __launch_bounds__(256) finalize_kernel(const __nv_bfloat16* __restrict__ rows_buf,
+                                                       const int32_t* __restrict__ token_rows,
+                                                       void* __restrict__ out, int T, int out_fp32) {
+  griddep_wait();
+  constexpr int kC8 = kHidden / 8;  // 896 eight-column chunks per token
+  const int64_t n = (int64_t)T * kC8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = static_cast<int>(i / kC8);
+    const int c8 = static_cast<int>(i - (int64_t)t * kC8);
+    float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
+    const int4* tr = reinterpret_cast<const int4*>(token_rows + (size_t)t * kTopK);
+    const int4 r0 = __ldg(tr), r1 = __ldg(tr + 1);
+    const int r[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      if (r[k] < 0) break;
+      // 8 bf16 columns of the row; bf16 -> f32 is exact (upper half of the word)
+      const uint4 q = __ldcs(reinterpret_cast<const uint4*>(rows_buf + (size_t)r[k] * kHidden) + c8);
+      s0.x += __uint_as_float(q.x << 16); s0.y += __uint_as_float(q.x & 0xFFFF0000u);
+      s0.z += __uint_as_float(q.y << 16); s0.w += __uint_as_float(q.y & 0xFFFF0000u);
+      s1.x += __uint_as_float(q.z << 16); s1.y += __uint_as_float(q.z & 0xFFFF0000u);
+      s1.z += __uint_as_float(q.w << 16); s1.w += __uint_as_float(q.w & 0xFFFF0000u);
+    }
+    if (out_fp32) {
+      float4* o = reinterpret_cast<float4*>(out) + 2 * i;
+      o[0] = s0;
+      o[1] = s1;
+    } else {
+      __nv_bfloat162 b0 = __floats2bfloat162_rn(s0.x, s0.y);
+      __nv_bfloat162 b1 = __floats2bfloat162_rn(s0.z, s0.w);
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(s1.x, s1.y);
+      __nv_bfloat162 b3 = __floats2bfloat162_rn(s1.z, s1.w);
+      uint4 u;
+      u.x = *reinterpret_cast<uint32_t*>(&b0);
+      u.y = *reinterpret_cast<uint32_t*>(&b1);
+      u.z = *reinterpret_cast<uint32_t*>(&b2);
+      u.w = *reinterpret_cast<uint32_t*>(&b3);
+      reinterpret_cast<uint4*>(out)[i] = u;
+    }
+  }
+}
+
 }  // namespace
 
 int device_sm_count() {
@@ -223,6 +289,21 @@ int route_ctas_for(int T, int ctas_per_sm) {
 cudaError_t launch_route(const Workspace& ws, const RouteArgs& a, cudaStream_t s) {
   const int grid = (a.T + a.tokens_per_cta - 1) / a.tokens_per_cta;
   return launch_k(route_plan_kernel, dim3(grid), dim3(kRouteThreads), 0, s, false, a, ws);
+}
+
+cudaError_t launch_permute(const Workspace& ws, const PermuteArgs& a, cudaStream_t s) {
+  if (a.T <= 0) return cudaSuccess;
+  return launch_k(permute_kernel, dim3((a.T + 7) / 8), dim3(256), 0, s, true, a, ws);
+}
+
+cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32, cudaStream_t s) {
+  const int64_t n8 = (int64_t)T * kHidden / 8;
+  if (n8 == 0) return cudaSuccess;
+  int64_t blocks = (n8 + 255) / 256;
+  if (blocks > 16 * kSMs) blocks = 16 * kSMs;
+  return launch_k(finalize_kernel, dim3((unsigned)blocks), dim3(256), 0, s, true,
+                  static_cast<const __nv_bfloat16*>(ws.out_rows), static_cast<const int32_t*>(ws.token_rows), out, T,
+                  out_fp32);
 }
 
 }  // namespace moe

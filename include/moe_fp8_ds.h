@@ -102,7 +102,7 @@ int moe_fp8_ds_route(const float* routing_logits, const void* routing_bias,
  * memory is owned by a fixed-size pool or arena, an engine that reserves all
  * memory at start-up, or code that must not take the CUDA allocator's locks on
  * its hot path). Same arguments, outputs and status codes as
- * moe_fp8_ds_route(), but all scratch lives in one fixed array of 790,272
+ * moe_fp8_ds_route(), but all scratch lives in one fixed array of 1,052,416
  * bytes in the library's own device memory, present on every GPU that loads
  * the library until the process exits; the call makes no allocation of any
  * kind. Limits: seq_len <= 8192 (larger requests return MOE_ERR_INVALID_ARG
@@ -147,7 +147,7 @@ int moe_fp8_ds_experts(const void* hidden_states, const float* hidden_states_sca
  * While enabled, every pipeline call records CUDA events on its own stream
  * around each of its kernels. moe_fp8_ds_profile_last() synchronises on the
  * last call's final event and writes the milliseconds of its kernels
- * (route, gemm1, gemm2) to ms_out[0..2]; returns the number
+ * (route, permute, gemm1, gemm2, finalize) to ms_out[0..4]; returns the number
  * written, or a negative status. A call served by the fused decode kernel
  * records one interval (that kernel) and returns 1. Disabled by default;
  * enabling costs one event record per kernel.
@@ -160,7 +160,7 @@ int moe_fp8_ds_profile_last(float* ms_out, int n);
  * 1 <= seq_len <= 64 (no reference counterpart: path selection of this
  * library). on = 1: one persistent kernel does routing, both GEMMs and the
  * combine. on = 0 (the default, unless the environment sets
- * MOE_FP8_DS_FUSED_DECODE=1): the three-kernel pipeline that larger calls use.
+ * MOE_FP8_DS_FUSED_DECODE=1): the kernel pipeline that larger calls use.
  * on < 0 only queries. Returns the previous setting. Both give results within
  * the same tolerance of the reference.
  */
@@ -240,15 +240,14 @@ int moe_fp8_ds_device_status(void* stream);
 /*
  * Diagnostic (no counterpart in the reference): where the last layer call on
  * this device with `num_local_experts` (moe_fp8_ds_kernel, _kernel_ex or
- * _experts) placed each token's expert rows. For token t < seq_len,
- * local_expert_out[t][j] (int32 [seq_len][8]) is its j-th local expert in
- * ascending id (-1 padded) and slot_out[t][j] the row's slot inside that
- * expert: slot s belongs to the expert's m-tile s / 128 of the grouped GEMMs.
- * seq_len must not exceed the last call's. Asynchronous device-to-device
- * copies on `stream`; tests use it to choose rows that cover every m-tile.
+ * _experts) placed each token's expert rows. rows_out int32 [seq_len][8]:
+ * row rows_out[t][j] of the expert-major padded layout holds token t for its
+ * j-th local expert in ascending id (-1 padded); the row belongs to m-tile
+ * row / 128 of the grouped GEMMs, and every m-tile to exactly one expert.
+ * seq_len must not exceed the last call's. An asynchronous device-to-device
+ * copy on `stream`; tests use it to choose rows that cover every m-tile.
  */
-int moe_fp8_ds_last_rows(int64_t seq_len, int64_t num_local_experts, int32_t* local_expert_out, int32_t* slot_out,
-                         void* stream);
+int moe_fp8_ds_last_rows(int64_t seq_len, int64_t num_local_experts, int32_t* rows_out, void* stream);
 
 /* Bytes of device workspace the library holds for (seq_len, num_local_experts). */
 size_t moe_fp8_ds_workspace_bytes(int64_t seq_len, int64_t num_local_experts);

@@ -1,5 +1,5 @@
 """GPU: the fused decode kernel (one persistent launch for calls with
-1..64 tokens) against the three-kernel pipeline and the CPU oracle.
+1..64 tokens) against the kernel pipeline and the CPU oracle.
 
 Both paths must route identically (ids, weights, counts bit-exact) and give
 outputs within the parity tolerance of the oracle; the fused path's scratch

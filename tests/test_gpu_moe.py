@@ -61,11 +61,10 @@ def _rows_covering_every_mtile(T, e_local, counts, n_min, seed):
     """Tokens whose expert rows together touch every m-tile of every local
     expert (first, last and partial ones included), from the row placement of
     the call just made, topped up with random tokens to at least n_min."""
-    le, sl = pkg().last_rows(T, e_local)
-    le, sl = le.cpu().numpy().astype(np.int64), sl.cpu().numpy().astype(np.int64)
-    ok = le >= 0
-    keys = (le * (1 << 20) + sl // 128)[ok]
-    toks = np.broadcast_to(np.arange(T)[:, None], le.shape)[ok]
+    rows_of = pkg().last_rows(T, e_local).cpu().numpy().astype(np.int64)
+    ok = rows_of >= 0
+    keys = (rows_of // 128)[ok]  # m-tile of each (token, local expert) row
+    toks = np.broadcast_to(np.arange(T)[:, None], rows_of.shape)[ok]
     uniq, first = np.unique(keys, return_index=True)
     n_tiles = int(sum((int(c) + 127) // 128 for c in counts))
     assert len(uniq) == n_tiles, (len(uniq), n_tiles)
