@@ -382,8 +382,8 @@ def _measure_layer(pkg, lib, dev, stream, flush, w, acts_cpu, e_local, steps, wa
 
 
 # Intervals moe_fp8_ds_profile_last reports, by their number.
-KERNEL_NAMES = {5: ("route", "permute", "gemm1", "gemm2", "finalize"), 3: ("route+permute", "gemm1", "gemm2+combine"),
-                1: ("fused_decode",)}
+KERNEL_NAMES = {5: ("route", "permute", "gemm1", "gemm2", "finalize"), 4: ("route+permute", "gemm1", "gemm2", "finalize"),
+                3: ("route+permute", "gemm1", "gemm2+combine"), 1: ("fused_decode",)}
 
 
 def _gemm1_ms(m, T):

@@ -1,6 +1,6 @@
 // moe_api.cu — the C ABI (include/moe_fp8_ds.h): argument checks, cached
 // device workspace, TMA tensor maps and the launch sequence
-//   route+plan -> permute -> GEMM1(+SwiGLU+requant) -> GEMM2(+combine) -> finalize
+//   route+plan+permute -> GEMM1(+SwiGLU+requant) -> GEMM2(+weight) -> finalize
 // on the caller's stream, with no host synchronisation.
 #include <cstdlib>
 #include <mutex>
@@ -90,7 +90,6 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // (self-resetting counters, the combine accumulator, split-K scratch).
 size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_bytes, bool routing_only = false) {
   const int64_t rows = routing_only ? 0 : rows_cap_for(T, e_local);
-  const int ctas = route_ctas_for(static_cast<int>(T));
   size_t off = 0;
   auto take = [&](size_t bytes) {
     size_t o = off;
@@ -100,6 +99,8 @@ size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_
   const size_t Tz = static_cast<size_t>(T > 0 ? T : 1);
   w.expert_fill = reinterpret_cast<int32_t*>(take((size_t)kExperts * 4));
   w.done_ctas = reinterpret_cast<uint32_t*>(take(4));
+  w.bar_cnt = reinterpret_cast<uint32_t*>(take(4));
+  w.leave_cnt = reinterpret_cast<uint32_t*>(take(4));
   w.status = reinterpret_cast<unsigned*>(take(4));
   if (routing_only) {
     if (zero_bytes) *zero_bytes = off;
@@ -107,11 +108,9 @@ size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_
     w.topk_ids = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
     w.topk_w = reinterpret_cast<float*>(take(Tz * kTopK * 4));
     w.topk_rank = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
-    w.cta_off = reinterpret_cast<int32_t*>(take((size_t)(ctas > 256 ? ctas : 256) * kExperts * 4));
     w.rows_cap = 0;
     w.t_cap = T;
     w.e_local = e_local;
-    w.route_ctas_cap = ctas;
     return off;
   }
   w.tile_sem = reinterpret_cast<int32_t*>(take((size_t)kMaxSplitMTiles * kNT1 * 4));
@@ -139,7 +138,6 @@ size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_
   w.topk_ids = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
   w.topk_w = reinterpret_cast<float*>(take(Tz * kTopK * 4));
   w.topk_rank = reinterpret_cast<int32_t*>(take(Tz * kTopK * 4));
-  w.cta_off = reinterpret_cast<int32_t*>(take((size_t)(ctas > 256 ? ctas : 256) * e_local * 4));
   w.a1 = take((size_t)rows * kHidden);
   w.a1_scale = reinterpret_cast<float*>(take((size_t)rows * kHiddenBlocks * 4));
   w.row_token = reinterpret_cast<int32_t*>(take((size_t)rows * 4));
@@ -149,7 +147,6 @@ size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_
   w.rows_cap = rows;
   w.t_cap = T;
   w.e_local = e_local;
-  w.route_ctas_cap = ctas;
   return off;
 }
 
@@ -210,8 +207,9 @@ int check_device() {
   return major_cache[dev] == 10 ? MOE_OK : MOE_ERR_NO_DEVICE;
 }
 
-// Optional per-kernel CUDA events (moe_fp8_ds_profile_enable).
-constexpr int kProfKernels = 5;
+// Optional per-kernel CUDA events (moe_fp8_ds_profile_enable): routing with
+// the permutation, GEMM1, GEMM2, finalize.
+constexpr int kProfKernels = 4;
 bool g_prof_on = false;
 bool g_prof_valid = false;
 int g_prof_n = kProfKernels;  // intervals recorded by the last call (1 for the fused decode kernel)
@@ -305,13 +303,14 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
   ra.offset = static_cast<int>(offset);
   ra.e_local = static_cast<int>(E_l);
   ra.scale = static_cast<float>(scale);
-  ra.tokens_per_cta = tokens_per_cta_for(static_cast<int>(T));
   ra.user_ids = user_ids;
   ra.user_w = user_w;
   ra.user_counts = user_counts;
-  if (!route_only) prof_mark(0, s);
-  if (launch_route(*ws, ra, s) != cudaSuccess) return MOE_ERR_CUDA;
-  if (route_only) return MOE_OK;
+  if (route_only) {
+    ra.tokens_per_cta = tokens_per_cta_for(static_cast<int>(T));
+    return launch_route(*ws, ra, s) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+  }
+  if (route_permute_grid(static_cast<int>(T), &ra.tokens_per_cta) < 1) return MOE_ERR_CUDA;
 
   // calls with at most 64 rows use the skinny GEMM configuration (64-row
   // token tiles, one more stage of weights in flight)
@@ -330,15 +329,15 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
   pa.T = static_cast<int>(T);
   pa.offset = static_cast<int>(offset);
   pa.tokens_per_cta = ra.tokens_per_cta;
+  prof_mark(0, s);
+  if (launch_route_permute(*ws, ra, pa, s) != cudaSuccess) return MOE_ERR_CUDA;
   prof_mark(1, s);
-  if (launch_permute(*ws, pa, s) != cudaSuccess) return MOE_ERR_CUDA;
-  prof_mark(2, s);
   if (launch_gemm1(*ws, ma1, mw1, s1, s, skinny) != cudaSuccess) return MOE_ERR_CUDA;
-  prof_mark(3, s);
+  prof_mark(2, s);
   if (launch_gemm2(*ws, ma2, mw2, s2, s, skinny) != cudaSuccess) return MOE_ERR_CUDA;
-  prof_mark(4, s);
+  prof_mark(3, s);
   if (launch_finalize(*ws, static_cast<int>(T), out, out_fp32, s) != cudaSuccess) return MOE_ERR_CUDA;
-  prof_mark(5, s);
+  prof_mark(4, s);
   g_prof_n = kProfKernels;
   g_prof_valid = g_prof_on;
   return MOE_OK;

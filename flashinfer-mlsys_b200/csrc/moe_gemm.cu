@@ -625,12 +625,14 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
 
 }  // namespace
 
-// The permutation kernel runs between the routing kernel and GEMM1, so both
-// GEMMs may read the plan before their programmatic-launch wait.
+// GEMM1 directly follows the routing kernel that writes the plan, so it reads
+// the plan after its programmatic-launch wait. GEMM2 was released by GEMM1
+// after that wait: the plan is complete when GEMM2 starts, and GEMM2 loads it
+// and issues its first weight tiles before waiting for GEMM1.
 cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
                          const float* w_scale, cudaStream_t s, bool skinny) {
-  return skinny ? launch_gemm<1, 1>(ws, map_a, map_w, w_scale, s, 1)
-                : launch_gemm<1, 0>(ws, map_a, map_w, w_scale, s, 1);
+  return skinny ? launch_gemm<1, 1>(ws, map_a, map_w, w_scale, s, 0)
+                : launch_gemm<1, 0>(ws, map_a, map_w, w_scale, s, 0);
 }
 
 cudaError_t launch_gemm2(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,

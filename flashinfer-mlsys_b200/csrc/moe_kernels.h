@@ -49,14 +49,14 @@ struct Workspace {
   int64_t t_cap = 0;       // tokens (rows of the caller's tensors) it was sized for
   int e_local = 0;         // local experts it was sized for
   int64_t rows_cap = 0;    // rows of the expert-major padded layout
-  int route_ctas_cap = 0;  // routing CTAs it was sized for
 
   int32_t* topk_ids = nullptr;     // [t_cap][8] global expert ids
   float* topk_w = nullptr;         // [t_cap][8]
   int32_t* topk_rank = nullptr;    // [t_cap][8] rank inside (routing CTA, expert), -1 = not local
-  int32_t* cta_off = nullptr;      // [route_ctas_cap][e_local] first slot of each CTA in an expert
   int32_t* expert_fill = nullptr;  // [e_local] running counters (self-resetting)
   uint32_t* done_ctas = nullptr;   // routing CTAs finished (self-resetting)
+  uint32_t* bar_cnt = nullptr;     // fused routing kernel: CTAs at the grid barrier (self-resetting)
+  uint32_t* leave_cnt = nullptr;   // fused routing kernel: CTAs past the barrier (self-resetting)
   Plan* plan = nullptr;
   uint8_t* a1 = nullptr;           // [rows_cap][7168] permuted e4m3 token rows
   float* a1_scale = nullptr;       // [56][rows_cap]
@@ -126,8 +126,12 @@ int route_ctas_for(int T, int ctas_per_sm = kRouteCtasPerSm);
 int device_sm_count();  // cached per device
 int tokens_per_cta_for(int T, int ctas_per_sm = kRouteCtasPerSm);
 
+// Routing alone (no permutation): route_ctas_for() CTAs, no CTA waits for another.
 cudaError_t launch_route(const Workspace& ws, const RouteArgs& a, cudaStream_t s);
-cudaError_t launch_permute(const Workspace& ws, const PermuteArgs& a, cudaStream_t s);
+// Routing fused with the permutation: one cooperative launch. The grid and
+// a.tokens_per_cta must come from route_permute_grid (-1: no device).
+int route_permute_grid(int T, int* tokens_per_cta);
+cudaError_t launch_route_permute(const Workspace& ws, const RouteArgs& a, const PermuteArgs& pa, cudaStream_t s);
 // skinny: every m-tile has at most kSkinnyMaxRows valid rows (map_a then has
 // kSkinnyMaxRows-row boxes)
 cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,

@@ -19,7 +19,7 @@ namespace {
 
 // Limits of the allocation-free router.
 constexpr int kNoAllocMaxTokens = 8192;
-constexpr int kNoAllocMaxCtas = 256;  // route_ctas_for(T, 1) <= 149 for any T
+constexpr int kNoAllocMaxCtas = 256;  // route_ctas_for(T, 1) <= 148 for any T <= 8192
 
 // Scratch layout inside the static array (byte offsets, 256-byte aligned).
 constexpr size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -31,9 +31,8 @@ constexpr size_t kOffPlan = kZeroBytes;                                         
 constexpr size_t kOffIds = kOffPlan + a256(sizeof(Plan));                       // int32 [T][8]
 constexpr size_t kOffW = kOffIds + a256((size_t)kNoAllocMaxTokens * kTopK * 4); // f32 [T][8]
 constexpr size_t kOffRank = kOffW + a256((size_t)kNoAllocMaxTokens * kTopK * 4);
-constexpr size_t kOffCtaOff = kOffRank + a256((size_t)kNoAllocMaxTokens * kTopK * 4);
-constexpr size_t kScratchBytes = kOffCtaOff + a256((size_t)kNoAllocMaxCtas * kExperts * 4);  // 1,052,416 B
-static_assert(kScratchBytes == 1052416, "the size stated in include/moe_fp8_ds.h");
+constexpr size_t kScratchBytes = kOffRank + a256((size_t)kNoAllocMaxTokens * kTopK * 4);  // 790,272 B
+static_assert(kScratchBytes == 790272, "the size stated in include/moe_fp8_ds.h");
 
 static __device__ __align__(256) unsigned char g_route_scratch[kScratchBytes];
 
@@ -97,7 +96,6 @@ extern "C" int moe_fp8_ds_route_noalloc(const float* routing_logits, const void*
   ws.topk_ids = reinterpret_cast<int32_t*>(b + kOffIds);
   ws.topk_w = reinterpret_cast<float*>(b + kOffW);
   ws.topk_rank = reinterpret_cast<int32_t*>(b + kOffRank);
-  ws.cta_off = reinterpret_cast<int32_t*>(b + kOffCtaOff);
 
   RouteArgs ra{};
   ra.logits = routing_logits;

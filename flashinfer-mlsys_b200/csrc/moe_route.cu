@@ -24,14 +24,15 @@ constexpr int kMinTokensPerCta = 8;
 #define MOE_SPLIT_UNIT_OVERHEAD 16
 #endif
 constexpr int kSplitUnitOverhead = MOE_SPLIT_UNIT_OVERHEAD;
+constexpr uint64_t kRouteWaitLimitNs = 2000000000ull;  // 2 s: only reached if something is broken
 
 // One warp, one token: copy the e4m3 row (7168 B) and its 56 block scales to
 // every local expert slot the token was routed to, and record the token's
-// rows. `prefix` is the m-tile prefix of the local experts.
+// rows. `prefix` is the m-tile prefix of the local experts, `base` the first
+// slot of the token's routing CTA inside every expert.
 __device__ __forceinline__ void permute_token(int t, int lane, const uint8_t* __restrict__ hidden,
                                               const float* __restrict__ hidden_scale, int T, int offset,
-                                              int tokens_per_cta, const int* prefix, const Workspace& ws) {
-  const int E_l = ws.e_local;
+                                              const int* prefix, const int* base, const Workspace& ws) {
   int row = -1;
   float w = 0.f;
   if (lane < kTopK) {
@@ -39,8 +40,7 @@ __device__ __forceinline__ void permute_token(int t, int lane, const uint8_t* __
     const int r = ws.topk_rank[o];
     if (r >= 0) {
       const int le = ws.topk_ids[o] - offset;
-      const int cta = t / tokens_per_cta;
-      row = prefix[le] * kTileM + ws.cta_off[(size_t)cta * E_l + le] + r;
+      row = prefix[le] * kTileM + base[le] + r;
       w = ws.topk_w[o];
     }
   }
@@ -85,73 +85,22 @@ __device__ __forceinline__ void permute_token(int t, int lane, const uint8_t* __
   }
 }
 
-__global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, Workspace ws) {
-  __shared__ int hist[kExperts];
-  __shared__ int is_last;
+// The device-side plan from the per-expert counts (thread e < E_l holds the
+// count `c` of local expert e): m-tile prefix (also left in `s_prefix`,
+// E_l + 1 entries), the number of (token, local expert) pairs and the K split
+// of both GEMMs. With `write`, the plan and the optional user counts are
+// stored. Called by every thread of the CTA.
+__device__ __forceinline__ void build_plan(int c, int E_l, int* s_prefix, bool write, int32_t* user_counts,
+                                           const Workspace& ws) {
+  __shared__ int warp_tot[2][kRouteThreads / 32];
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int E_l = a.e_local;
-  // first kernel of a call: launched with normal stream ordering; let the
-  // permutation kernel get scheduled early (it waits for this grid).
-  griddep_launch_dependents();
-  for (int e = tid; e < E_l; e += blockDim.x) hist[e] = 0;
-  __syncthreads();
-
-  const int t_begin = blockIdx.x * a.tokens_per_cta;
-  const int t_end = min(a.T, t_begin + a.tokens_per_cta);
   const int nwarps = blockDim.x >> 5;
-  for (int t = t_begin + warp; t < t_end; t += nwarps) {
-    int my_id = -1;     // lane k < 8 holds the k-th selected expert
-    float my_w = 0.f;
-    if (a.logits != nullptr) {
-      route_token_warp(a.logits + (size_t)t * kExperts, a.bias, a.scale, lane, my_id, my_w);
-    } else if (lane < kTopK) {
-      my_id = __ldg(a.given_ids + (size_t)t * kTopK + lane);
-      my_w = __ldg(a.given_w + (size_t)t * kTopK + lane);
-    }
-    if (lane < kTopK) {
-      const size_t o = (size_t)t * kTopK + lane;
-      ws.topk_ids[o] = my_id;
-      ws.topk_w[o] = my_w;
-      if (a.user_ids) a.user_ids[o] = my_id;
-      if (a.user_w) a.user_w[o] = my_w;
-      const int le = my_id - a.offset;
-      int r = -1;
-      if (my_id >= 0 && le >= 0 && le < E_l) r = atomicAdd(&hist[le], 1);
-      ws.topk_rank[o] = r;
-    }
-  }
-  __syncthreads();
-
-  int c = 0;
-  if (gridDim.x == 1) {
-    // single CTA: the shared histogram is the whole story
-    if (tid < E_l) {
-      c = hist[tid];
-      ws.cta_off[tid] = 0;
-    }
-  } else {
-    // ---- publish this CTA's histogram: its base slot inside every expert ----
-    for (int e = tid; e < E_l; e += blockDim.x) {
-      const int h = hist[e];
-      ws.cta_off[(size_t)blockIdx.x * E_l + e] = h ? atomicAdd(&ws.expert_fill[e], h) : 0;
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) is_last = (atomicAdd(ws.done_ctas, 1u) == gridDim.x - 1) ? 1 : 0;
-    __syncthreads();
-    if (!is_last) return;
-    // ---- last CTA: per-expert counts ----
-    __threadfence();
-    if (tid < E_l) c = atomicExch(&ws.expert_fill[tid], 0);  // read and reset for the next call
-  }
-  // ---- m-tile prefix and K-split plan ----
-  __shared__ int warp_tot[2][kRouteThreads / 32];
-  if (tid < E_l) {
+  if (write && tid < E_l) {
     ws.plan->count[tid] = c;
-    if (a.user_counts) a.user_counts[tid] = c;
+    if (user_counts) user_counts[tid] = c;
   }
-  int m = (c + kTileM - 1) / kTileM;
+  const int m = (c + kTileM - 1) / kTileM;
   // block-wide exclusive scan of m-tiles and total of rows over the experts
   int incl = m, csum = c;
 #pragma unroll
@@ -169,8 +118,12 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
     total += warp_tot[0][w];
     nas += warp_tot[1][w];
   }
-  if (tid < E_l) ws.plan->mtile_prefix[tid] = base + incl - m;
-  if (warp == 0) {
+  if (tid < E_l) {
+    s_prefix[tid] = base + incl - m;
+    if (write) ws.plan->mtile_prefix[tid] = base + incl - m;
+  }
+  if (tid == 0) s_prefix[E_l] = total;
+  if (write && warp == 0) {
     // K split: minimise waves * (K blocks per unit + per-unit overhead); lane = split - 1
     auto cost = [&](int tiles, int nkb, int smax, int sp) -> long long {
       if (sp > smax || tiles <= 0) return 0x7fffffffffffLL;
@@ -196,18 +149,154 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
       ws.plan->n_assign = nas;
       ws.plan->split1 = total > 0 ? static_cast<int>(k1 & 0xFF) : 1;
       ws.plan->split2 = total > 0 ? static_cast<int>(k2 & 0xFF) : 1;
-      *ws.done_ctas = 0u;
+    }
+  }
+  __syncthreads();
+}
+
+// Routes the CTA's tokens (one warp per token) and counts its local
+// assignments per expert in `hist`; writes ids, weights and per-(CTA, expert)
+// ranks to the workspace and the optional user outputs.
+__device__ __forceinline__ void route_tokens(const RouteArgs& a, const Workspace& ws, int* hist, int t_begin,
+                                             int t_end) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  for (int t = t_begin + warp; t < t_end; t += nwarps) {
+    int my_id = -1;     // lane k < 8 holds the k-th selected expert
+    float my_w = 0.f;
+    if (a.logits != nullptr) {
+      route_token_warp(a.logits + (size_t)t * kExperts, a.bias, a.scale, lane, my_id, my_w);
+    } else if (lane < kTopK) {
+      my_id = __ldg(a.given_ids + (size_t)t * kTopK + lane);
+      my_w = __ldg(a.given_w + (size_t)t * kTopK + lane);
+    }
+    if (lane < kTopK) {
+      const size_t o = (size_t)t * kTopK + lane;
+      ws.topk_ids[o] = my_id;
+      ws.topk_w[o] = my_w;
+      if (a.user_ids) a.user_ids[o] = my_id;
+      if (a.user_w) a.user_w[o] = my_w;
+      const int le = my_id - a.offset;
+      int r = -1;
+      if (my_id >= 0 && le >= 0 && le < a.e_local) r = atomicAdd(&hist[le], 1);
+      ws.topk_rank[o] = r;
     }
   }
 }
 
-__global__ void __launch_bounds__(256) permute_kernel(PermuteArgs a, Workspace ws) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 8 + warp;
-  griddep_wait();
+// Routing alone (moe_fp8_ds_route and the allocation-free router): the last
+// CTA to finish builds the plan, so no CTA ever waits for another.
+__global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, Workspace ws) {
+  __shared__ int hist[kExperts];
+  __shared__ int s_prefix[kExperts + 1];
+  __shared__ int is_last;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int E_l = a.e_local;
+  for (int e = tid; e < E_l; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
+
+  const int t_begin = blockIdx.x * a.tokens_per_cta;
+  const int t_end = min(a.T, t_begin + a.tokens_per_cta);
+  route_tokens(a, ws, hist, t_begin, t_end);
+  __syncthreads();
+
+  int c = 0;
+  if (gridDim.x == 1) {
+    // single CTA: the shared histogram is the whole story
+    if (tid < E_l) c = hist[tid];
+  } else {
+    // ---- publish this CTA's histogram ----
+    for (int e = tid; e < E_l; e += blockDim.x) {
+      const int h = hist[e];
+      if (h) atomicAdd(&ws.expert_fill[e], h);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) is_last = (atomicAdd(ws.done_ctas, 1u) == gridDim.x - 1) ? 1 : 0;
+    __syncthreads();
+    if (!is_last) return;
+    // ---- last CTA: per-expert counts ----
+    __threadfence();
+    if (tid < E_l) c = atomicExch(&ws.expert_fill[tid], 0);  // read and reset for the next call
+  }
+  build_plan(c, E_l, s_prefix, true, a.user_counts, ws);
+  if (tid == 0) *ws.done_ctas = 0u;
+}
+
+// Routing fused with the histogram, the prefix sum and the token
+// permutation (kernel.cu:157-232, ref_moe.py:95-148) in one cooperative launch
+// (every CTA is resident). Each CTA routes its tokens, takes its base slot
+// inside every expert from the running per-expert counters, and meets the
+// others at a grid barrier; then every CTA reads the final counts, computes
+// the m-tile prefix itself and copies its own tokens' e4m3 rows and scales to
+// their slots of the expert-major padded layout. CTA 0 writes the plan the
+// GEMMs read. The barrier wait is bounded (status bit and no permutation on
+// timeout); the last CTA to leave resets the counters for the next call.
+__global__ void __launch_bounds__(kRouteThreads) route_permute_kernel(RouteArgs a, PermuteArgs pa, Workspace ws) {
+  __shared__ int hist[kExperts];
+  __shared__ int s_base[kExperts];
+  __shared__ int s_prefix[kExperts + 1];
+  __shared__ int s_ok;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int E_l = a.e_local;
+  const int G = gridDim.x;
+  // first kernel of a call: let GEMM1 get scheduled early (it runs its
+  // prologue, then waits for this grid)
   griddep_launch_dependents();
-  if (t >= a.T) return;
-  permute_token(t, lane, a.hidden, a.hidden_scale, a.T, a.offset, a.tokens_per_cta, ws.plan->mtile_prefix, ws);
+  for (int e = tid; e < E_l; e += blockDim.x) hist[e] = 0;
+  if (tid == 0) s_ok = 1;
+  __syncthreads();
+  const int t_begin = blockIdx.x * a.tokens_per_cta;
+  const int t_end = min(a.T, t_begin + a.tokens_per_cta);
+  route_tokens(a, ws, hist, t_begin, t_end);
+  __syncthreads();
+  int c = 0;
+  if (G == 1) {
+    for (int e = tid; e < E_l; e += blockDim.x) s_base[e] = 0;
+    if (tid < E_l) c = hist[tid];
+  } else {
+    for (int e = tid; e < E_l; e += blockDim.x) {
+      const int h = hist[e];
+      s_base[e] = h ? atomicAdd(&ws.expert_fill[e], h) : 0;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      atomicAdd(ws.bar_cnt, 1u);
+      bool ok = true;
+      uint64_t t0 = 0;
+      for (uint32_t spin = 0;; ++spin) {
+        uint32_t v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ws.bar_cnt) : "memory");
+        if (v >= static_cast<uint32_t>(G)) break;
+        if (spin == 0) t0 = global_timer_ns();
+        else if (global_timer_ns() - t0 > kRouteWaitLimitNs) { ok = false; break; }
+        __nanosleep(64);
+      }
+      if (!ok) {
+        atomicOr(ws.status, kErrTimeout);
+        s_ok = 0;
+      }
+    }
+    __syncthreads();
+    if (tid < E_l) c = __ldcg(&ws.expert_fill[tid]);
+  }
+  build_plan(c, E_l, s_prefix, blockIdx.x == 0, a.user_counts, ws);
+  if (s_ok) {
+    for (int t = t_begin + warp; t < t_end; t += kRouteThreads / 32)
+      permute_token(t, lane, pa.hidden, pa.hidden_scale, pa.T, pa.offset, s_prefix, s_base, ws);
+  }
+  if (G > 1) {
+    __syncthreads();
+    if (tid == 0 && atomicAdd(ws.leave_cnt, 1u) == static_cast<uint32_t>(G) - 1) {
+      // every CTA has read the counts: reset them for the next call
+      for (int e = 0; e < E_l; ++e) ws.expert_fill[e] = 0;
+      *ws.bar_cnt = 0u;
+      *ws.leave_cnt = 0u;
+    }
+  }
 }
 
 // out[t, :] = sum over the token's local rows (ascending expert id) of the
@@ -291,9 +380,40 @@ cudaError_t launch_route(const Workspace& ws, const RouteArgs& a, cudaStream_t s
   return launch_k(route_plan_kernel, dim3(grid), dim3(kRouteThreads), 0, s, false, a, ws);
 }
 
-cudaError_t launch_permute(const Workspace& ws, const PermuteArgs& a, cudaStream_t s) {
-  if (a.T <= 0) return cudaSuccess;
-  return launch_k(permute_kernel, dim3((a.T + 7) / 8), dim3(256), 0, s, true, a, ws);
+int route_permute_grid(int T, int* tokens_per_cta) {
+  // all CTAs must be resident at once (cooperative launch): at most as many
+  // as the device holds, up to kRouteCtasPerSm per SM
+  static int occ_cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+  if (!occ_cache[dev]) {
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, route_permute_kernel, kRouteThreads, 0) != cudaSuccess ||
+        occ < 1)
+      return -1;
+    occ_cache[dev] = occ < kRouteCtasPerSm ? occ : kRouteCtasPerSm;
+  }
+  const int ctas = device_sm_count() * occ_cache[dev];
+  int per = (T + ctas - 1) / ctas;
+  per = ((per + 7) / 8) * 8;
+  if (per < kMinTokensPerCta) per = kMinTokensPerCta;
+  *tokens_per_cta = per;
+  return (T + per - 1) / per;
+}
+
+cudaError_t launch_route_permute(const Workspace& ws, const RouteArgs& a, const PermuteArgs& pa, cudaStream_t s) {
+  const int grid = (a.T + a.tokens_per_cta - 1) / a.tokens_per_cta;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kRouteThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = grid > 1 ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, route_permute_kernel, a, pa, ws);
 }
 
 cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32, cudaStream_t s) {

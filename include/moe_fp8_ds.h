@@ -102,7 +102,7 @@ int moe_fp8_ds_route(const float* routing_logits, const void* routing_bias,
  * memory is owned by a fixed-size pool or arena, an engine that reserves all
  * memory at start-up, or code that must not take the CUDA allocator's locks on
  * its hot path). Same arguments, outputs and status codes as
- * moe_fp8_ds_route(), but all scratch lives in one fixed array of 1,052,416
+ * moe_fp8_ds_route(), but all scratch lives in one fixed array of 790,272
  * bytes in the library's own device memory, present on every GPU that loads
  * the library until the process exits; the call makes no allocation of any
  * kind. Limits: seq_len <= 8192 (larger requests return MOE_ERR_INVALID_ARG
@@ -147,7 +147,7 @@ int moe_fp8_ds_experts(const void* hidden_states, const float* hidden_states_sca
  * While enabled, every pipeline call records CUDA events on its own stream
  * around each of its kernels. moe_fp8_ds_profile_last() synchronises on the
  * last call's final event and writes the milliseconds of its kernels
- * (route, permute, gemm1, gemm2, finalize) to ms_out[0..4]; returns the number
+ * (route with the permutation, gemm1, gemm2, finalize) to ms_out[0..3]; returns the number
  * written, or a negative status. A call served by the fused decode kernel
  * records one interval (that kernel) and returns 1. Disabled by default;
  * enabling costs one event record per kernel.
