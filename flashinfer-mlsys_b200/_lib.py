@@ -37,6 +37,7 @@ SIGNATURES = {
     "moe_fp8_ds_profile_enable": (ctypes.c_int, [ctypes.c_int]),
     "moe_fp8_ds_profile_last": (ctypes.c_int, [ctypes.POINTER(ctypes.c_float), ctypes.c_int]),
     "moe_fp8_ds_set_fused_decode": (ctypes.c_int, [ctypes.c_int]),
+    "moe_fp8_ds_test_route_barrier": (ctypes.c_int, [ctypes.c_uint64, ctypes.c_int]),
     "moe_fp8_ds_quantize_act": (ctypes.c_int, [_vp, _c_int64, _vp, _vp, _vp]),
     "moe_fp8_ds_add_norm_quant": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_float, _c_int64, _vp, _vp, _vp]),
     "moe_fp8_ds_ep_pack": (ctypes.c_int, [_vp, _vp, _vp, _vp, _c_int64, _vp, _c_int64, _vp, _vp]),

@@ -232,6 +232,10 @@ bool fused_decode_enabled() {
   return g_fused_decode == 1;
 }
 
+// Failure-path test hook (moe_fp8_ds_test_route_barrier), off by default.
+uint64_t g_test_wait_limit_ns = 0;
+int g_test_skip_arrival = -1;
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 bool valid_e_local(int64_t e) { return e == 32 || e == 64 || e == 128 || e == 256; }
@@ -311,6 +315,8 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
     return launch_route(*ws, ra, s) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
   }
   if (route_permute_grid(static_cast<int>(T), &ra.tokens_per_cta) < 1) return MOE_ERR_CUDA;
+  ra.wait_limit_ns = g_test_wait_limit_ns;
+  ra.skip_arrival_cta = g_test_skip_arrival;
 
   // calls with at most 64 rows use the skinny GEMM configuration (64-row
   // token tiles, one more stage of weights in flight)
@@ -580,6 +586,13 @@ int moe_fp8_ds_profile_last(float* ms_out, int n) {
     if (cudaEventElapsedTime(&ms_out[i], g_prof_ev[i], g_prof_ev[i + 1]) != cudaSuccess) return -MOE_ERR_CUDA;
   }
   return k;
+}
+
+int moe_fp8_ds_test_route_barrier(uint64_t wait_limit_ns, int skip_arrival_cta) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_test_wait_limit_ns = wait_limit_ns;
+  g_test_skip_arrival = skip_arrival_cta;
+  return MOE_OK;
 }
 
 int moe_fp8_ds_set_fused_decode(int on) {

@@ -90,6 +90,11 @@ struct RouteArgs {
   int32_t* user_ids;          // optional outputs
   float* user_w;
   int32_t* user_counts;
+  // Fused routing kernel: the grid-barrier wait limit (0 = the default) and
+  // a CTA that skips its barrier arrival (-1 = none). Set only by the
+  // failure-path test hook moe_fp8_ds_test_route_barrier.
+  uint64_t wait_limit_ns;
+  int skip_arrival_cta;
 };
 
 struct PermuteArgs {

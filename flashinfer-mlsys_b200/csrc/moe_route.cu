@@ -263,8 +263,9 @@ __global__ void __launch_bounds__(kRouteThreads) route_permute_kernel(RouteArgs 
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) {
+    if (tid == 0 && static_cast<int>(blockIdx.x) != a.skip_arrival_cta) {
       atomicAdd(ws.bar_cnt, 1u);
+      const uint64_t limit = a.wait_limit_ns ? a.wait_limit_ns : kRouteWaitLimitNs;
       bool ok = true;
       uint64_t t0 = 0;
       for (uint32_t spin = 0;; ++spin) {
@@ -272,13 +273,15 @@ __global__ void __launch_bounds__(kRouteThreads) route_permute_kernel(RouteArgs 
         asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ws.bar_cnt) : "memory");
         if (v >= static_cast<uint32_t>(G)) break;
         if (spin == 0) t0 = global_timer_ns();
-        else if (global_timer_ns() - t0 > kRouteWaitLimitNs) { ok = false; break; }
+        else if (global_timer_ns() - t0 > limit) { ok = false; break; }
         __nanosleep(64);
       }
       if (!ok) {
         atomicOr(ws.status, kErrTimeout);
         s_ok = 0;
       }
+    } else if (tid == 0) {
+      s_ok = 0;  // test hook: this CTA stays away from the barrier
     }
     __syncthreads();
     if (tid < E_l) c = __ldcg(&ws.expert_fill[tid]);
@@ -287,6 +290,11 @@ __global__ void __launch_bounds__(kRouteThreads) route_permute_kernel(RouteArgs 
   if (s_ok) {
     for (int t = t_begin + warp; t < t_end; t += kRouteThreads / 32)
       permute_token(t, lane, pa.hidden, pa.hidden_scale, pa.T, pa.offset, s_prefix, s_base, ws);
+  } else {
+    // the barrier gave up: no rows for these tokens (the finalize writes
+    // zeros; the GEMMs only read rows inside the padded layout)
+    for (int t = t_begin + warp; t < t_end; t += kRouteThreads / 32)
+      if (lane < kTopK) ws.token_rows[(size_t)t * kTopK + lane] = -1;
   }
   if (G > 1) {
     __syncthreads();

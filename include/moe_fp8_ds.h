@@ -167,6 +167,18 @@ int moe_fp8_ds_profile_last(float* ms_out, int n);
 int moe_fp8_ds_set_fused_decode(int on);
 
 /*
+ * Failure-path test hook (no counterpart in the reference; off by default).
+ * Calls with more than 8 tokens route in one cooperative kernel whose CTAs
+ * meet at a grid barrier with a bounded wait (2 s). wait_limit_ns > 0 lowers
+ * that limit; skip_arrival_cta >= 0 makes that CTA stay away from the
+ * barrier, so the others give up after the limit, set the device status bit
+ * and return without permuting (the call's output is then undefined and
+ * moe_fp8_ds_device_status reports MOE_ERR_DEVICE_TIMEOUT and clears the
+ * counters). (0, -1) restores normal operation.
+ */
+int moe_fp8_ds_test_route_barrier(uint64_t wait_limit_ns, int skip_arrival_cta);
+
+/*
  * The step upstream of the layer (no counterpart in the reference's solution;
  * its harness supplies pre-quantised inputs, reference moe/ref_moe.json:57-80):
  * BF16 hidden states [seq_len][7168] -> hidden_fp8_out e4m3 [seq_len][7168]
