@@ -113,8 +113,8 @@ size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_
     w.e_local = e_local;
     return off;
   }
-  w.tile_sem = reinterpret_cast<int32_t*>(take((size_t)kMaxSplitMTiles * kNT1 * 4));
-  w.tile_sem2 = reinterpret_cast<int32_t*>(take((size_t)kMaxSplitMTiles * kNT2 * 4));
+  w.tile_sem = reinterpret_cast<int32_t*>(take((size_t)kMaxSplitMTiles * kNT1 * 4 * 4));
+  w.tile_sem2 = reinterpret_cast<int32_t*>(take((size_t)kMaxSplitMTiles * kNT2 * kEpiWarps * 4));
   w.g_part = reinterpret_cast<float*>(take((size_t)kMaxSplitMTiles * kTileM * kGemm1N * 4));
   w.g2_part = reinterpret_cast<float*>(take((size_t)kMaxSplitMTiles * kTileM * kHidden * 4));
   // fused decode kernel scratch (independent of T)
@@ -322,8 +322,11 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
   // token tiles, one more stage of weights in flight)
   const bool skinny = T <= kSkinnyMaxRows;
   const uint32_t a_box = skinny ? kSkinnyMaxRows : kTileM;
+  // small calls: GEMM1 gathers its few rows straight from hidden_states
+  // (one-row boxes), so the routing kernel copies no rows
   CUtensorMap ma1, mw1, ma2, mw2;
-  if (!make_map(&ma1, ws->a1, kHidden, ws->rows_cap, a_box) ||
+  if (!(skinny ? make_map(&ma1, hidden, kHidden, static_cast<uint64_t>(T), 1)
+               : make_map(&ma1, ws->a1, kHidden, ws->rows_cap, a_box)) ||
       !make_map(&mw1, w1, kHidden, static_cast<uint64_t>(E_l) * kGemm1N) ||
       !make_map(&ma2, ws->inter, kInterCols, ws->rows_cap, a_box) ||
       !make_map(&mw2, w2, kInter, static_cast<uint64_t>(E_l) * kHidden))
@@ -335,10 +338,11 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
   pa.T = static_cast<int>(T);
   pa.offset = static_cast<int>(offset);
   pa.tokens_per_cta = ra.tokens_per_cta;
+  pa.copy_rows = skinny ? 0 : 1;
   prof_mark(0, s);
   if (launch_route_permute(*ws, ra, pa, s) != cudaSuccess) return MOE_ERR_CUDA;
   prof_mark(1, s);
-  if (launch_gemm1(*ws, ma1, mw1, s1, s, skinny) != cudaSuccess) return MOE_ERR_CUDA;
+  if (launch_gemm1(*ws, ma1, mw1, s1, s, skinny, hidden_scale, T) != cudaSuccess) return MOE_ERR_CUDA;
   prof_mark(2, s);
   if (launch_gemm2(*ws, ma2, mw2, s2, s, skinny) != cudaSuccess) return MOE_ERR_CUDA;
   prof_mark(3, s);

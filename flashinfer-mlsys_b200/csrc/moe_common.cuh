@@ -166,6 +166,19 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Four rows y0..y3 of a 2D tensor map whose box is one row high (x: 128
+// bytes at column x) into four consecutive 128-byte rows of shared memory;
+// the 128-byte swizzle follows the destination address, so row i lands as
+// row (dst/128 + i) of its 1024-byte swizzle atom. Plain load (no multicast).
+__device__ __forceinline__ void tma_gather4(void* smem_dst, const CUtensorMap* map, int x, int y0, int y1, int y2,
+                                            int y3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cta.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5, %6}], [%7];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -37,17 +37,23 @@ namespace {
 struct GemmArgs {
   const Plan* plan;
   const float* a_scale;     // GEMM1: [56][rows_cap]; GEMM2: [16][rows_cap]
+  // GEMM1 of calls with at most 64 tokens gathers its rows from
+  // hidden_states instead: the token of every padded row and the [56][T]
+  // activation scales
+  const int32_t* row_token;
+  const float* x_scale;
+  int64_t x_ld;
   const float* w_scale;     // GEMM1: [E_l][32][56];  GEMM2: [E_l][56][16]
   int rows_cap;
   int e_local;
   uint8_t* inter;           // GEMM1 out: [rows_cap][4096]
   float* inter_scale;       // GEMM1 out: [16][rows_cap]
   float* g_part;            // GEMM1 split-K scratch: [kMaxSplitMTiles*128][4096]
-  int32_t* tile_sem;        // GEMM1 split-K counters: [kMaxSplitMTiles][16]
+  int32_t* tile_sem;        // GEMM1 split-K counters: [kMaxSplitMTiles][16][4 lane quarters]
   const float* row_weight;  // GEMM2: routing weight of each permuted row
   __nv_bfloat16* out_rows;  // GEMM2 out: [rows_cap][7168] weighted expert outputs (bf16)
   float* g2_part;           // GEMM2 split-K scratch: [kMaxSplitMTiles*128][7168]
-  int32_t* tile_sem2;       // GEMM2 split-K counters: [kMaxSplitMTiles][28]
+  int32_t* tile_sem2;       // GEMM2 split-K counters: [kMaxSplitMTiles][28][16 epilogue warps]
   unsigned* status;
   int plan_early;           // 1: the plan was complete before the previous kernel released this one
 };
@@ -98,7 +104,6 @@ struct __align__(16) SmemCtl {
   uint64_t epi_bar;   // barrier among the 16 epilogue warps (bounded waits)
   uint32_t tmem_base;
   int abort_flag;
-  int fixup_flag;
   int plan_total;      // total m-tiles of the call
   int plan_split;      // K split of this GEMM
   int prefix[kExperts + 1];
@@ -163,33 +168,35 @@ __device__ __forceinline__ float e4m3_byte_to_f32(uint32_t b) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu)));
 }
 
-// SwiGLU of 32 (gate, up) pairs of one row + two-term e4m3 quantisation of the
-// 128-wide intermediate block shared by the 4 column-group warps of the row.
-__device__ __forceinline__ void swiglu_quant_store(const float* gate, const float* up, int cg, int row_in_tile,
-                                                   bool valid, size_t row, int n, SmemCtl* ctl,
-                                                   const GemmArgs& p, EpiSync& es) {
-  // padding rows (past the expert's token count) hold garbage partials; keep
-  // them out of expf/division, whose special-value paths would stall the warp
-  float c[32];
+// SwiGLU of N (gate, up) pairs of one row, in place (gate[i] becomes the
+// intermediate value), and their absolute maximum. Padding rows (past the
+// expert's token count) hold garbage partials; they are kept out of the
+// exponential and reciprocal, whose special-value paths would stall the warp.
+template <int N>
+__device__ __forceinline__ float swiglu_n(float* gate, const float* up, bool valid) {
   float amax = 0.f;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
+  for (int i = 0; i < N; ++i) {
     const float g = valid ? gate[i] : 0.f;
     const float u = valid ? up[i] : 0.f;
-    c[i] = g * silu_ref(u);
-    amax = fmaxf(amax, fabsf(c[i]));
+    gate[i] = g * silu_ref(u);
+    amax = fmaxf(amax, fabsf(gate[i]));
   }
-  ctl->amax[cg][row_in_tile] = amax;
-  if (!es.sync(ctl, p.status)) return;
-  amax = fmaxf(fmaxf(ctl->amax[0][row_in_tile], ctl->amax[1][row_in_tile]),
-               fmaxf(ctl->amax[2][row_in_tile], ctl->amax[3][row_in_tile]));
-  if (!es.sync(ctl, p.status)) return;
-  if (!valid) return;
+  return amax;
+}
+
+// Two-term e4m3 quantisation of N intermediate values of padded row `row`,
+// columns n * 128 + col .. + N, with the amax of their 128-wide block:
+// hi = e4m3(c / s), lo = e4m3(c / s - hi), s = amax / 448; the piece at
+// column 0 also stores the block's scale.
+template <int N>
+__device__ __forceinline__ void quant_store_n(const float* c, float amax, size_t row, int n, int col,
+                                              const GemmArgs& p) {
   const float inv = amax > 0.f ? 448.0f / amax : 0.f;
   const float scale = amax / 448.0f;
-  uint32_t hi_w[8], lo_w[8];
+  uint32_t hi_w[N / 4], lo_w[N / 4];
 #pragma unroll
-  for (int i = 0; i < 32; i += 4) {
+  for (int i = 0; i < N; i += 4) {
     uint32_t hw = 0, lw = 0;
 #pragma unroll
     for (int j = 0; j < 4; j += 2) {
@@ -203,14 +210,76 @@ __device__ __forceinline__ void swiglu_quant_store(const float* gate, const floa
     hi_w[i / 4] = hw;
     lo_w[i / 4] = lw;
   }
-  uint8_t* base = p.inter + row * kInterCols + n * kBlk + cg * 32;
+  uint8_t* base = p.inter + row * kInterCols + n * kBlk + col;
   uint4* dh = reinterpret_cast<uint4*>(base);
   uint4* dl = reinterpret_cast<uint4*>(base + kInter);
-  dh[0] = make_uint4(hi_w[0], hi_w[1], hi_w[2], hi_w[3]);
-  dh[1] = make_uint4(hi_w[4], hi_w[5], hi_w[6], hi_w[7]);
-  dl[0] = make_uint4(lo_w[0], lo_w[1], lo_w[2], lo_w[3]);
-  dl[1] = make_uint4(lo_w[4], lo_w[5], lo_w[6], lo_w[7]);
-  if (cg == 0) p.inter_scale[(size_t)n * p.rows_cap + row] = scale;
+#pragma unroll
+  for (int i = 0; i < N / 16; ++i) {
+    dh[i] = make_uint4(hi_w[4 * i], hi_w[4 * i + 1], hi_w[4 * i + 2], hi_w[4 * i + 3]);
+    dl[i] = make_uint4(lo_w[4 * i], lo_w[4 * i + 1], lo_w[4 * i + 2], lo_w[4 * i + 3]);
+  }
+  if (col == 0) p.inter_scale[(size_t)n * p.rows_cap + row] = scale;
+}
+
+// SwiGLU of 32 (gate, up) pairs of one row + two-term e4m3 quantisation of the
+// 128-wide intermediate block shared by the 4 column-group warps of the row
+// (their amax meets in shared memory).
+__device__ __forceinline__ void swiglu_quant_store(float* gate, const float* up, int cg, int row_in_tile,
+                                                   bool valid, size_t row, int n, SmemCtl* ctl,
+                                                   const GemmArgs& p, EpiSync& es) {
+  float amax = swiglu_n<32>(gate, up, valid);
+  ctl->amax[cg][row_in_tile] = amax;
+  if (!es.sync(ctl, p.status)) return;
+  amax = fmaxf(fmaxf(ctl->amax[0][row_in_tile], ctl->amax[1][row_in_tile]),
+               fmaxf(ctl->amax[2][row_in_tile], ctl->amax[3][row_in_tile]));
+  if (!es.sync(ctl, p.status)) return;
+  if (valid) quant_store_n<32>(gate, amax, row, n, cg * 32, p);
+}
+
+// Split GEMM1, after the last partial of one TMEM lane quarter (rows
+// q*32 .. q*32+31 of m-tile gm, n-tile n) has arrived: the finished sums are
+// read back from the fp32 scratch (which is cleared for the next call) and
+// turned into the two-term intermediate. Eight lanes per row (lane & 7 picks
+// 16 of the 128 columns), four rows per pass; the block amax meets by
+// shuffles, so no other warp takes part. `buf` holds 32 floats of scratch.
+__device__ __forceinline__ void fixup_quarter_g1(const GemmArgs& p, int gm, int n, int rows, int q, int lane,
+                                                 float* buf) {
+  const int r_end = min(rows, q * 32 + 32);
+  const int col = (lane & 7) * 16;
+  for (int rb = q * 32; rb < r_end; rb += 4) {
+    const int r = rb + (lane >> 3);
+    const bool valid = r < r_end;
+    const size_t row = (size_t)gm * kTileM + r;
+    if (valid) {
+      float4* pg = reinterpret_cast<float4*>(p.g_part + row * kGemm1N + n * kBlk + col);
+      float4* pu = reinterpret_cast<float4*>(p.g_part + row * kGemm1N + kInter + n * kBlk + col);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 a4 = __ldcg(pg + i), b4 = __ldcg(pu + i);
+        buf[4 * i] = a4.x; buf[4 * i + 1] = a4.y; buf[4 * i + 2] = a4.z; buf[4 * i + 3] = a4.w;
+        buf[16 + 4 * i] = b4.x; buf[17 + 4 * i] = b4.y; buf[18 + 4 * i] = b4.z; buf[19 + 4 * i] = b4.w;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __stcg(pg + i, make_float4(0.f, 0.f, 0.f, 0.f));
+        __stcg(pu + i, make_float4(0.f, 0.f, 0.f, 0.f));
+      }
+    }
+    float amax = swiglu_n<16>(buf, buf + 16, valid);
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+    if (valid) quant_store_n<16>(buf, amax, row, n, col, p);
+  }
+}
+
+// Bytes one pipeline stage receives: the two weight slabs plus the token
+// tile(s); GEMM1 of small calls gathers its rows in groups of four (the last
+// group repeats the unit's last row) instead of loading a 64-row box.
+template <int kMode, int kSkinny>
+__device__ __forceinline__ uint32_t stage_tx_bytes(int rows) {
+  if (kMode == 1 && kSkinny) return static_cast<uint32_t>(kStageB + ((rows + 3) >> 2) * 4 * kBlk);
+  return static_cast<uint32_t>(GemmCfg<kMode, kSkinny>::kStageBytes);
 }
 
 template <int kMode, int kSkinny>
@@ -283,7 +352,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const Unit x = decode_unit<kMode>(u, split0, ctl->prefix, ctl->count, E_l);
       for (int kb = x.kb0; kb < x.kb1 && n_pre < kStages; ++kb, ++n_pre) {
         uint8_t* sb = tiles + n_pre * kStageBytes + kBOff;
-        mbar_arrive_expect_tx(&ctl->full[n_pre], kStageBytes);
+        mbar_arrive_expect_tx(&ctl->full[n_pre], stage_tx_bytes<kMode, kSkinny>(x.rows));
         if (kMode == 1) {
           const int y0 = x.e * kGemm1N + x.n * kBlk;
           tma_load_2d(sb, &map_w, kb * kBlk, y0, &ctl->full[n_pre]);
@@ -309,7 +378,52 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int units = total_mtiles * NT * split;
   const uint32_t tmem = ctl->tmem_base;
 
-  if (warp == 0) {
+  constexpr bool kGather = (kMode == 1 && kSkinny == 1);
+  if (warp == 0 && kGather) {
+    // ============ TMA producer, rows gathered from hidden_states ============
+    // lane 0 waits for a free stage and loads the weights; lane l gathers
+    // rows 4l..4l+3 of the unit (tile::gather4, one-row boxes)
+    uint32_t it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      if (__shfl_sync(0xffffffffu, aborted(ctl) ? 1 : 0, 0)) break;
+      const Unit x = decode_unit<kMode>(u, split, ctl->prefix, ctl->count, E_l);
+      const int ngroups = (x.rows + 3) >> 2;
+      int y[4] = {0, 0, 0, 0};
+      if (lane < ngroups) {
+        const int32_t* rt = p.row_token + (size_t)x.gm * kTileM;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) y[i] = __ldg(rt + min(4 * lane + i, x.rows - 1));
+      }
+      for (int kb = x.kb0; kb < x.kb1; ++kb, ++it) {
+        const int s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1u;
+        uint8_t* sa = tiles + s * kStageBytes;
+        if (lane == 0 && static_cast<int>(it) >= n_pre) {
+          ok = mbar_wait_bounded(&ctl->empty[s], ph ^ 1u, kWaitLimitNs);
+          if (ok) {
+            mbar_arrive_expect_tx(&ctl->full[s], stage_tx_bytes<kMode, kSkinny>(x.rows));
+            const int y0 = x.e * kGemm1N + x.n * kBlk;
+            tma_load_2d(sa + kBOff, &map_w, kb * kBlk, y0, &ctl->full[s]);
+            tma_load_2d(sa + kBOff + kStageA, &map_w, kb * kBlk, y0 + kInter, &ctl->full[s]);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
+        if (lane < ngroups) tma_gather4(sa + lane * 4 * kBlk, &map_a, kb * kBlk, y[0], y[1], y[2], y[3], &ctl->full[s]);
+      }
+      if (!ok) break;
+    }
+    if (lane == 0) {
+      if (!ok) signal_abort(ctl, p.status);
+      if (aborted(ctl)) {
+        // drain: wait (bounded) for the loads this warp may still have in flight
+        const uint32_t n_issued = it > static_cast<uint32_t>(n_pre) ? it : static_cast<uint32_t>(n_pre);
+        for (uint32_t j = (n_issued > (uint32_t)kStages ? n_issued - kStages : 0); j < n_issued; ++j)
+          mbar_wait_bounded(&ctl->full[j % kStages], (j / kStages) & 1u, kWaitLimitNs);
+      }
+    }
+  } else if (warp == 0) {
     // ======================= TMA producer =======================
     if (lane == 0) {
       uint32_t it = 0;
@@ -394,6 +508,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t it = 0;
     for (int u = blockIdx.x; u < units && !aborted(ctl); u += gridDim.x) {
       const Unit x = decode_unit<kMode>(u, split, ctl->prefix, ctl->count, E_l);
+      // gathered GEMM1 rows: the tokens of rows 4l..4l+3 (-1 past the last row)
+      int y[4] = {-1, -1, -1, -1};
+      if (kGather) {
+        const int32_t* rt = p.row_token + (size_t)x.gm * kTileM;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (4 * lane + i < x.rows) y[i] = __ldg(rt + 4 * lane + i);
+      }
       bool ok = true;
       for (int kb = x.kb0; kb < x.kb1; ++kb, ++it) {
         const int j = it % kScaleSlots;
@@ -405,7 +527,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         ScaleSlot* sl = &ctl->scales[j];
         const int ka = kb;
-        cp_async_16(&sl->a[4 * lane], p.a_scale + (size_t)ka * p.rows_cap + (size_t)x.gm * kTileM + 4 * lane);
+        if (kGather) {
+          // hidden_states_scale [56][T]: block kb of each gathered token
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (y[i] >= 0) cp_async_4(&sl->a[4 * lane + i], p.x_scale + (size_t)kb * p.x_ld + y[i]);
+        } else {
+          cp_async_16(&sl->a[4 * lane], p.a_scale + (size_t)ka * p.rows_cap + (size_t)x.gm * kTileM + 4 * lane);
+        }
         if (lane < 2) {
           const float* src;
           if (kMode == 1)
@@ -488,8 +617,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // one call site of the SwiGLU stage (its code is fetched once)
         bool do_swiglu = (split == 1);
         if (split > 1) {
-          // split-K: reduce promoted partials in fp32 scratch; the last
-          // arriving CTA of this (m-tile, n-tile) runs SwiGLU + quantisation.
+          // split-K: promoted partials meet in fp32 scratch. Arrivals are
+          // counted per (m-tile, n-tile, lane quarter) over the 4 column-group
+          // warps of every split; the last warp to arrive finishes that
+          // quarter's rows (no barrier among the epilogue warps).
           float* g = p.g_part + row * kGemm1N;
           if (valid) {
 #pragma unroll
@@ -500,32 +631,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
           __threadfence();
-          if (!es.sync(ctl, p.status)) break;
-          if (warp == kEpiWarp0 && lane == 0) {
-            const int old = atomicAdd(&p.tile_sem[x.gm * kNT1 + x.n], 1);
-            ctl->fixup_flag = (old == split - 1) ? 1 : 0;
-          }
-          if (!es.sync(ctl, p.status)) break;
-          if (ctl->fixup_flag) {
+          __syncwarp();
+          int32_t* sem = p.tile_sem + ((size_t)x.gm * kNT1 + x.n) * 4 + q;
+          int last = 0;
+          if (lane == 0) last = (atomicAdd(sem, 1) == 4 * split - 1) ? 1 : 0;
+          last = __shfl_sync(0xffffffffu, last, 0);
+          if (last) {
             __threadfence();
-            if (valid) {
-              // all loads first (independent), then clear the scratch
-              float4* pg = reinterpret_cast<float4*>(g + x.n * kBlk + cg * 32);
-              float4* pu = reinterpret_cast<float4*>(g + kInter + x.n * kBlk + cg * 32);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float4 a4 = __ldcg(pg + i), b4 = __ldcg(pu + i);
-                acc[4 * i] = a4.x; acc[4 * i + 1] = a4.y; acc[4 * i + 2] = a4.z; acc[4 * i + 3] = a4.w;
-                acc[32 + 4 * i] = b4.x; acc[33 + 4 * i] = b4.y; acc[34 + 4 * i] = b4.z; acc[35 + 4 * i] = b4.w;
-              }
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                __stcg(pg + i, make_float4(0.f, 0.f, 0.f, 0.f));
-                __stcg(pu + i, make_float4(0.f, 0.f, 0.f, 0.f));
-              }
-            }
-            if (warp == kEpiWarp0 && lane == 0) p.tile_sem[x.gm * kNT1 + x.n] = 0;
-            do_swiglu = true;
+            if (lane == 0) *sem = 0;
+            fixup_quarter_g1(p, x.gm, x.n, x.rows, q, lane, acc);
           }
         }
         if (do_swiglu) swiglu_quant_store(acc, acc + 32, cg, row_in_tile, valid, row, x.n, ctl, p, es);
@@ -538,8 +652,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int i = 0; i < 64; i += 16) store_bf16x16(dst + i, w, acc + i);
           }
         } else {
-          // split-K: partial sums meet in fp32 scratch; the last arriving CTA
-          // of this (m-tile, n-tile) writes the finished rows.
+          // split-K: partial sums meet in fp32 scratch. Arrivals are counted
+          // per (m-tile, n-tile, epilogue warp); the last split to arrive
+          // writes that warp's 32 rows x 64 columns.
           float* g = p.g2_part + row * kHidden + x.n * kTileN + cg * 64;
           if (valid) {
 #pragma unroll
@@ -547,14 +662,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               red_add_v4(g + i, w * acc[i], w * acc[i + 1], w * acc[i + 2], w * acc[i + 3]);
           }
           __threadfence();
-          if (!es.sync(ctl, p.status)) break;
-          if (warp == kEpiWarp0 && lane == 0) {
-            const int old = atomicAdd(&p.tile_sem2[x.gm * kNT2 + x.n], 1);
-            ctl->fixup_flag = (old == split - 1) ? 1 : 0;
-          }
-          if (!es.sync(ctl, p.status)) break;
-          if (ctl->fixup_flag) {
+          __syncwarp();
+          int32_t* sem = p.tile_sem2 + ((size_t)x.gm * kNT2 + x.n) * kEpiWarps + (warp - kEpiWarp0);
+          int last = 0;
+          if (lane == 0) last = (atomicAdd(sem, 1) == split - 1) ? 1 : 0;
+          last = __shfl_sync(0xffffffffu, last, 0);
+          if (last) {
             __threadfence();
+            if (lane == 0) *sem = 0;
             if (valid) {
               // all loads first (independent), then the stores
               float4* pg = reinterpret_cast<float4*>(g);
@@ -568,7 +683,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
               for (int i = 0; i < 64; i += 16) store_bf16x16(dst + i, 1.0f, acc + i);
             }
-            if (warp == kEpiWarp0 && lane == 0) p.tile_sem2[x.gm * kNT2 + x.n] = 0;
           }
         }
       }
@@ -588,7 +702,8 @@ size_t gemm_smem_bytes() { return kRingBytes + sizeof(SmemCtl) + 1024; }
 
 template <int kMode, int kSkinny>
 cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
-                        const float* w_scale, cudaStream_t s, int plan_early) {
+                        const float* w_scale, cudaStream_t s, int plan_early, const float* x_scale = nullptr,
+                        int64_t x_ld = 0) {
   // The shared-memory opt-in is a per-device function attribute: one bit per
   // device that has it (launches run under the library's host mutex).
   static uint64_t configured = 0;
@@ -615,6 +730,9 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
   p.g_part = ws.g_part;
   p.tile_sem = ws.tile_sem;
   p.row_weight = ws.row_weight;
+  p.row_token = ws.row_token;
+  p.x_scale = x_scale;
+  p.x_ld = x_ld;
   p.out_rows = ws.out_rows;
   p.g2_part = ws.g2_part;
   p.tile_sem2 = ws.tile_sem2;
@@ -630,8 +748,8 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
 // after that wait: the plan is complete when GEMM2 starts, and GEMM2 loads it
 // and issues its first weight tiles before waiting for GEMM1.
 cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
-                         const float* w_scale, cudaStream_t s, bool skinny) {
-  return skinny ? launch_gemm<1, 1>(ws, map_a, map_w, w_scale, s, 0)
+                         const float* w_scale, cudaStream_t s, bool skinny, const float* x_scale, int64_t T) {
+  return skinny ? launch_gemm<1, 1>(ws, map_a, map_w, w_scale, s, 0, x_scale, T)
                 : launch_gemm<1, 0>(ws, map_a, map_w, w_scale, s, 0);
 }
 

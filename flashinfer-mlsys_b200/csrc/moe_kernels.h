@@ -65,9 +65,9 @@ struct Workspace {
   uint8_t* inter = nullptr;        // [rows_cap][4096] two-term e4m3 intermediate (hi | lo)
   float* inter_scale = nullptr;    // [16][rows_cap] hi scales (lo = hi / 16)
   float* g_part = nullptr;         // [kMaxSplitMTiles*128][4096] GEMM1 split-K partial sums (kept zero)
-  int32_t* tile_sem = nullptr;     // [kMaxSplitMTiles][16] GEMM1 split-K arrival counters (kept zero)
+  int32_t* tile_sem = nullptr;     // [kMaxSplitMTiles][16][4] GEMM1 split-K arrival counters (kept zero)
   float* g2_part = nullptr;        // [kMaxSplitMTiles*128][7168] GEMM2 split-K partial sums (kept zero)
-  int32_t* tile_sem2 = nullptr;    // [kMaxSplitMTiles][28] GEMM2 split-K arrival counters (kept zero)
+  int32_t* tile_sem2 = nullptr;    // [kMaxSplitMTiles][28][16] GEMM2 split-K arrival counters (kept zero)
   __nv_bfloat16* out_rows = nullptr;  // [rows_cap][7168] routing-weighted expert output of every permuted row (bf16)
   int32_t* token_rows = nullptr;   // [t_cap][8] permuted rows of each token, ascending expert id, -1 padded
   unsigned* status = nullptr;      // device status word (kErrTimeout ...)
@@ -103,6 +103,7 @@ struct PermuteArgs {
   int T;
   int offset;
   int tokens_per_cta;
+  int copy_rows;              // 0: record the row maps only (GEMM1 gathers the rows itself)
 };
 
 // Launch `kernel` on `s`; with `pdl` the launch may overlap the tail of the
@@ -137,10 +138,12 @@ cudaError_t launch_route(const Workspace& ws, const RouteArgs& a, cudaStream_t s
 // a.tokens_per_cta must come from route_permute_grid (-1: no device).
 int route_permute_grid(int T, int* tokens_per_cta);
 cudaError_t launch_route_permute(const Workspace& ws, const RouteArgs& a, const PermuteArgs& pa, cudaStream_t s);
-// skinny: every m-tile has at most kSkinnyMaxRows valid rows (map_a then has
-// kSkinnyMaxRows-row boxes)
+// skinny: every m-tile has at most kSkinnyMaxRows valid rows. GEMM1 then
+// gathers its rows from hidden_states (map_a: hidden_states [T][7168] with
+// one-row boxes, x_scale its [56][T] scales); otherwise map_a is the permuted
+// rows with 128-row boxes. GEMM2's map_a has kSkinnyMaxRows-row boxes when skinny.
 cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
-                         const float* w_scale, cudaStream_t s, bool skinny);
+                         const float* w_scale, cudaStream_t s, bool skinny, const float* x_scale, int64_t T);
 cudaError_t launch_gemm2(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
                          const float* w_scale, cudaStream_t s, bool skinny);
 cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32, cudaStream_t s);

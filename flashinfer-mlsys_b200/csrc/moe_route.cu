@@ -32,7 +32,8 @@ constexpr uint64_t kRouteWaitLimitNs = 2000000000ull;  // 2 s: only reached if s
 // slot of the token's routing CTA inside every expert.
 __device__ __forceinline__ void permute_token(int t, int lane, const uint8_t* __restrict__ hidden,
                                               const float* __restrict__ hidden_scale, int T, int offset,
-                                              const int* prefix, const int* base, const Workspace& ws) {
+                                              const int* prefix, const int* base, const Workspace& ws,
+                                              bool copy_rows) {
   int row = -1;
   float w = 0.f;
   if (lane < kTopK) {
@@ -64,20 +65,22 @@ __device__ __forceinline__ void permute_token(int t, int lane, const uint8_t* __
   const unsigned has = __ballot_sync(0xffffffffu, row >= 0);
   if (!has) return;
   const uint4* src = reinterpret_cast<const uint4*>(hidden + (size_t)t * kHidden);
-  const float sc0 = __ldg(hidden_scale + (size_t)lane * T + t);
-  const float sc1 = (lane + 32 < kHiddenBlocks) ? __ldg(hidden_scale + (size_t)(lane + 32) * T + t) : 0.f;
+  const float sc0 = copy_rows ? __ldg(hidden_scale + (size_t)lane * T + t) : 0.f;
+  const float sc1 = (copy_rows && lane + 32 < kHiddenBlocks) ? __ldg(hidden_scale + (size_t)(lane + 32) * T + t) : 0.f;
   unsigned m = has;
   while (m) {
     const int k = __ffs(m) - 1;
     m &= m - 1;
     const int r = __shfl_sync(0xffffffffu, row, k);
     const float wk = __shfl_sync(0xffffffffu, w, k);
-    // 14 chunks of 16 B per lane; repeated destinations re-read the row from L1
-    uint4* dst = reinterpret_cast<uint4*>(ws.a1 + (size_t)r * kHidden);
+    if (copy_rows) {
+      // 14 chunks of 16 B per lane; repeated destinations re-read the row from L1
+      uint4* dst = reinterpret_cast<uint4*>(ws.a1 + (size_t)r * kHidden);
 #pragma unroll 7
-    for (int i = 0; i < kHidden / 16 / 32; ++i) dst[lane + 32 * i] = __ldg(src + lane + 32 * i);
-    ws.a1_scale[(size_t)lane * ws.rows_cap + r] = sc0;
-    if (lane + 32 < kHiddenBlocks) ws.a1_scale[(size_t)(lane + 32) * ws.rows_cap + r] = sc1;
+      for (int i = 0; i < kHidden / 16 / 32; ++i) dst[lane + 32 * i] = __ldg(src + lane + 32 * i);
+      ws.a1_scale[(size_t)lane * ws.rows_cap + r] = sc0;
+      if (lane + 32 < kHiddenBlocks) ws.a1_scale[(size_t)(lane + 32) * ws.rows_cap + r] = sc1;
+    }
     if (lane == 0) {
       ws.row_token[r] = t;
       ws.row_weight[r] = wk;
@@ -289,7 +292,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_permute_kernel(RouteArgs 
   build_plan(c, E_l, s_prefix, blockIdx.x == 0, a.user_counts, ws);
   if (s_ok) {
     for (int t = t_begin + warp; t < t_end; t += kRouteThreads / 32)
-      permute_token(t, lane, pa.hidden, pa.hidden_scale, pa.T, pa.offset, s_prefix, s_base, ws);
+      permute_token(t, lane, pa.hidden, pa.hidden_scale, pa.T, pa.offset, s_prefix, s_base, ws, pa.copy_rows != 0);
   } else {
     // the barrier gave up: no rows for these tokens (the finalize writes
     // zeros; the GEMMs only read rows inside the padded layout)
