@@ -64,11 +64,13 @@ struct Unit {
   int e, m, n, gm, kb0, kb1, rows;
 };
 
-// Expert, m-tile and n-tile of tile `tile` (tiles are numbered m-tile major).
 template <int kMode>
-__device__ __forceinline__ Unit tile_unit(int tile, const int* prefix, const int* count, int e_local) {
+__device__ __forceinline__ Unit decode_unit(int u, int split, const int* prefix, const int* count, int e_local) {
   constexpr int NT = GemmCfg<kMode>::kNT;
+  constexpr int NKB = GemmCfg<kMode>::kNKB;
   Unit x;
+  const int ks = u % split;
+  const int tile = u / split;
   x.n = tile % NT;
   x.gm = tile / NT;
   // last expert whose first m-tile is <= gm (empty experts share prefixes)
@@ -80,71 +82,9 @@ __device__ __forceinline__ Unit tile_unit(int tile, const int* prefix, const int
   x.e = lo;
   x.m = x.gm - prefix[lo];
   x.rows = min(kTileM, count[lo] - x.m * kTileM);
+  x.kb0 = (ks * NKB) / split;
+  x.kb1 = ((ks + 1) * NKB) / split;
   return x;
-}
-
-// The work of one CTA as a list of pieces (a tile and a range of its K
-// blocks), kept in shared memory:
-//   split >= 1: uniform K split; piece i is unit blockIdx.x + i * gridDim.x of
-//     the (tile, K part) decomposition, and every tile has `split` pieces.
-//   split == 0: stream-K; the K blocks of all tiles, tile after tile, are dealt
-//     to the CTAs in equal contiguous ranges [c*KT/G, (c+1)*KT/G). Piece i is
-//     the i-th tile this CTA's range touches; a tile has as many pieces as
-//     CTAs whose range touches it.
-struct Sched {
-  int split, tiles, kt, k0, k1;
-};
-
-__device__ __forceinline__ int sk_start(int c, int kt) {
-  return static_cast<int>((long long)c * kt / gridDim.x);
-}
-
-// The CTA whose stream-K range holds global K block k.
-__device__ __forceinline__ int sk_owner(int k, int kt) {
-  const int G = gridDim.x;
-  int c = static_cast<int>((long long)k * G / kt);
-  while (c + 1 < G && sk_start(c + 1, kt) <= k) ++c;
-  while (c > 0 && sk_start(c, kt) > k) --c;
-  return c;
-}
-
-template <int kMode>
-__device__ __forceinline__ void make_sched(Sched* s, int total_mtiles, int split) {
-  constexpr int NT = GemmCfg<kMode>::kNT;
-  constexpr int NKB = GemmCfg<kMode>::kNKB;
-  s->split = split;
-  s->tiles = total_mtiles * NT;
-  s->kt = s->tiles * NKB;
-  s->k0 = split > 0 ? 0 : sk_start(blockIdx.x, s->kt);
-  s->k1 = split > 0 ? 0 : sk_start(blockIdx.x + 1, s->kt);
-}
-
-// Piece i of this CTA (false past the last); np = pieces of its tile.
-template <int kMode>
-__device__ __forceinline__ bool get_piece(const Sched* s, int i, const int* prefix, const int* count, int e_local,
-                                          Unit& x, int& np) {
-  constexpr int NKB = GemmCfg<kMode>::kNKB;
-  const int split = s->split;
-  if (split > 0) {
-    const int u = blockIdx.x + i * gridDim.x;
-    if (u >= s->tiles * split) return false;
-    const int ks = u % split;
-    x = tile_unit<kMode>(u / split, prefix, count, e_local);
-    x.kb0 = (ks * NKB) / split;
-    x.kb1 = ((ks + 1) * NKB) / split;
-    np = split;
-    return true;
-  }
-  const int k0 = s->k0, k1 = s->k1;
-  if (k0 >= k1) return false;
-  const int t = k0 / NKB + i;
-  const int kb_lo = t * NKB;
-  if (t >= s->tiles || kb_lo >= k1) return false;
-  x = tile_unit<kMode>(t, prefix, count, e_local);
-  x.kb0 = (k0 > kb_lo ? k0 : kb_lo) - kb_lo;
-  x.kb1 = (k1 < kb_lo + NKB ? k1 : kb_lo + NKB) - kb_lo;
-  np = sk_owner(kb_lo + NKB - 1, s->kt) - sk_owner(kb_lo, s->kt) + 1;
-  return true;
 }
 
 struct __align__(16) ScaleSlot {
@@ -165,8 +105,7 @@ struct __align__(16) SmemCtl {
   uint32_t tmem_base;
   int abort_flag;
   int plan_total;      // total m-tiles of the call
-  int plan_split;      // K split of this GEMM (0: stream-K)
-  Sched sched;         // this CTA's pieces
+  int plan_split;      // K split of this GEMM
   int prefix[kExperts + 1];
   int count[kExperts];
   float amax[4][kTileM];
@@ -349,6 +288,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     GemmArgs p) {
   using Cfg = GemmCfg<kMode, kSkinny>;
   static_assert(Cfg::kRing <= kRingBytes && Cfg::kStages <= kMaxStages, "stage ring does not fit");
+  constexpr int NT = Cfg::kNT;
   constexpr int kStages = Cfg::kStages;
   constexpr int kStageBytes = Cfg::kStageBytes;
   constexpr int kABytes = Cfg::kABytes;
@@ -406,11 +346,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   int n_pre = 0;
   if (p.plan_early && tid == 0) {
-    make_sched<kMode>(&ctl->sched, ctl->plan_total, ctl->plan_split);
-    Unit x;
-    int np;
-    for (int pi = 0; n_pre < kStages && get_piece<kMode>(&ctl->sched, pi, ctl->prefix, ctl->count, E_l, x, np);
-         ++pi) {
+    const int split0 = ctl->plan_split;
+    const int units0 = ctl->plan_total * NT * split0;
+    for (int u = blockIdx.x; u < units0 && n_pre < kStages; u += gridDim.x) {
+      const Unit x = decode_unit<kMode>(u, split0, ctl->prefix, ctl->count, E_l);
       for (int kb = x.kb0; kb < x.kb1 && n_pre < kStages; ++kb, ++n_pre) {
         uint8_t* sb = tiles + n_pre * kStageBytes + kBOff;
         mbar_arrive_expect_tx(&ctl->full[n_pre], stage_tx_bytes<kMode, kSkinny>(x.rows));
@@ -433,10 +372,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     load_plan();
     __syncthreads();
   }
-  if (tid == 0 && !p.plan_early) make_sched<kMode>(&ctl->sched, ctl->plan_total, ctl->plan_split);
-  __syncthreads();
 
-  const Sched* sch = &ctl->sched;
+  const int total_mtiles = ctl->plan_total;
+  const int split = ctl->plan_split;
+  const int units = total_mtiles * NT * split;
   const uint32_t tmem = ctl->tmem_base;
 
   constexpr bool kGather = (kMode == 1 && kSkinny == 1);
@@ -446,10 +385,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // rows 4l..4l+3 of the unit (tile::gather4, one-row boxes)
     uint32_t it = 0;
     bool ok = true;
-    Unit x;
-    int np;
-    for (int pi = 0; get_piece<kMode>(sch, pi, ctl->prefix, ctl->count, E_l, x, np); ++pi) {
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
       if (__shfl_sync(0xffffffffu, aborted(ctl) ? 1 : 0, 0)) break;
+      const Unit x = decode_unit<kMode>(u, split, ctl->prefix, ctl->count, E_l);
       const int ngroups = (x.rows + 3) >> 2;
       int y[4] = {0, 0, 0, 0};
       if (lane < ngroups) {
@@ -489,9 +427,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ======================= TMA producer =======================
     if (lane == 0) {
       uint32_t it = 0;
-      Unit x;
-      int np;
-      for (int pi = 0; !aborted(ctl) && get_piece<kMode>(sch, pi, ctl->prefix, ctl->count, E_l, x, np); ++pi) {
+      for (int u = blockIdx.x; u < units && !aborted(ctl); u += gridDim.x) {
+        const Unit x = decode_unit<kMode>(u, split, ctl->prefix, ctl->count, E_l);
         for (int kb = x.kb0; kb < x.kb1; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1u;
@@ -529,9 +466,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       constexpr uint32_t idesc = idesc_e4m3_f32(kTileM, kTileN);
       uint32_t it = 0, gkb = 0;
       bool issued_any = false;
-      Unit x;
-      int np;
-      for (int pi = 0; !aborted(ctl) && get_piece<kMode>(sch, pi, ctl->prefix, ctl->count, E_l, x, np); ++pi) {
+      for (int u = blockIdx.x; u < units && !aborted(ctl); u += gridDim.x) {
+        const Unit x = decode_unit<kMode>(u, split, ctl->prefix, ctl->count, E_l);
         for (int kb = x.kb0; kb < x.kb1; ++kb, ++it, ++gkb) {
           const uint32_t buf = gkb & 1u;
           if (!mbar_wait_bounded(&ctl->tempty[buf], ((gkb >> 1) & 1u) ^ 1u, kWaitLimitNs)) {
@@ -570,10 +506,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == kScaleWarp) {
     // ======================= scale loader =======================
     uint32_t it = 0;
-    Unit x;
-    int np;
-    for (int pi = 0; get_piece<kMode>(sch, pi, ctl->prefix, ctl->count, E_l, x, np); ++pi) {
-      if (__shfl_sync(0xffffffffu, aborted(ctl) ? 1 : 0, 0)) break;
+    for (int u = blockIdx.x; u < units && !aborted(ctl); u += gridDim.x) {
+      const Unit x = decode_unit<kMode>(u, split, ctl->prefix, ctl->count, E_l);
       // gathered GEMM1 rows: the tokens of rows 4l..4l+3 (-1 past the last row)
       int y[4] = {-1, -1, -1, -1};
       if (kGather) {
@@ -623,10 +557,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t gkb = 0;
     EpiSync es;
     float acc[64];
-    Unit x;
-    int np;
-    for (int pi = 0; get_piece<kMode>(sch, pi, ctl->prefix, ctl->count, E_l, x, np); ++pi) {
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
       if (aborted(ctl)) break;
+      const Unit x = decode_unit<kMode>(u, split, ctl->prefix, ctl->count, E_l);
       const size_t row = (size_t)x.gm * kTileM + row_in_tile;
       const bool valid = row_in_tile < x.rows;
 #pragma unroll
@@ -682,8 +615,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
       if (kMode == 1) {
         // one call site of the SwiGLU stage (its code is fetched once)
-        bool do_swiglu = (np == 1);
-        if (np > 1) {
+        bool do_swiglu = (split == 1);
+        if (split > 1) {
           // split-K: promoted partials meet in fp32 scratch. Arrivals are
           // counted per (m-tile, n-tile, lane quarter) over the 4 column-group
           // warps of every split; the last warp to arrive finishes that
@@ -701,7 +634,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           __syncwarp();
           int32_t* sem = p.tile_sem + ((size_t)x.gm * kNT1 + x.n) * 4 + q;
           int last = 0;
-          if (lane == 0) last = (atomicAdd(sem, 1) == 4 * np - 1) ? 1 : 0;
+          if (lane == 0) last = (atomicAdd(sem, 1) == 4 * split - 1) ? 1 : 0;
           last = __shfl_sync(0xffffffffu, last, 0);
           if (last) {
             __threadfence();
@@ -713,7 +646,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       } else {
         const float w = valid ? __ldg(p.row_weight + row) : 0.f;
         __nv_bfloat16* dst = p.out_rows + row * kHidden + x.n * kTileN + cg * 64;
-        if (np == 1) {
+        if (split == 1) {
           if (valid) {
 #pragma unroll
             for (int i = 0; i < 64; i += 16) store_bf16x16(dst + i, w, acc + i);
@@ -732,7 +665,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           __syncwarp();
           int32_t* sem = p.tile_sem2 + ((size_t)x.gm * kNT2 + x.n) * kEpiWarps + (warp - kEpiWarp0);
           int last = 0;
-          if (lane == 0) last = (atomicAdd(sem, 1) == np - 1) ? 1 : 0;
+          if (lane == 0) last = (atomicAdd(sem, 1) == split - 1) ? 1 : 0;
           last = __shfl_sync(0xffffffffu, last, 0);
           if (last) {
             __threadfence();

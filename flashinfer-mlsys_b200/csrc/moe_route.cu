@@ -24,12 +24,6 @@ constexpr int kMinTokensPerCta = 8;
 #define MOE_SPLIT_UNIT_OVERHEAD 16
 #endif
 constexpr int kSplitUnitOverhead = MOE_SPLIT_UNIT_OVERHEAD;
-// Small calls (at most kMaxSplitMTiles m-tiles) deal the K blocks of all tiles
-// to the CTAs in equal ranges (stream-K) instead of a uniform split.
-#ifndef MOE_STREAMK
-#define MOE_STREAMK 1
-#endif
-constexpr bool kStreamK = MOE_STREAMK != 0;
 constexpr uint64_t kRouteWaitLimitNs = 2000000000ull;  // 2 s: only reached if something is broken
 
 // One warp, one token: copy the e4m3 row (7168 B) and its 56 block scales to
@@ -156,11 +150,8 @@ __device__ __forceinline__ void build_plan(int c, int E_l, int* s_prefix, bool w
       ws.plan->mtile_prefix[E_l] = total;
       ws.plan->total_mtiles = total;
       ws.plan->n_assign = nas;
-      // small calls: stream-K (split 0), every CTA an equal share of the K
-      // blocks of all tiles; larger ones: the uniform split of least cost
-      const bool sk = kStreamK && total > 0 && total <= kMaxSplitMTiles;
-      ws.plan->split1 = sk ? 0 : (total > 0 ? static_cast<int>(k1 & 0xFF) : 1);
-      ws.plan->split2 = sk ? 0 : (total > 0 ? static_cast<int>(k2 & 0xFF) : 1);
+      ws.plan->split1 = total > 0 ? static_cast<int>(k1 & 0xFF) : 1;
+      ws.plan->split2 = total > 0 ? static_cast<int>(k2 & 0xFF) : 1;
     }
   }
   __syncthreads();
