@@ -51,6 +51,8 @@ WORKLOADS = {
     "decode_sweep": ((1, 2, 4, 8, 16, 32, 64), "BASELINE configs[1]: decode sweep, 32 local experts, offset 0"),
     "mid": ((256, 1024), "BASELINE configs[2]: mid prefill, near-uniform routing"),
     "large": ((4096, 8192, 16384), "BASELINE configs[3]: large prefill, +2.0 bias on 4 hot local experts"),
+    "shared": ((1, 8, 64, 1024, 4096), "DeepSeek-V3's shared expert fused into the layer (moe_fp8_ds_kernel_shared, "
+                                       "32 local experts) against the routed layer plus a separate shared-expert call"),
     "quant": ((1, 64, 4096, 16384), "upstream step: BF16 -> FP8 1x128 activation quantisation "
                                     "(moe_fp8_ds_quantize_act), bf16 ~N(0,1) hidden states"),
     "addnorm": ((1, 64, 4096, 16384), "downstream step: residual add + DeepSeek-V3 RMSNorm + FP8 1x128 "
@@ -861,6 +863,66 @@ def bench_quant(args):
     print(json.dumps(line), flush=True)
 
 
+def bench_shared(args):
+    """The shared expert fused into the layer's persistent GEMMs, against the
+    routed-only layer and against running it separately: per T, µs of
+    (a) the routed layer, (b) the fused call, (c) a shared-expert-only call of
+    the same entry (a routing bias that sends no token to a local expert), so
+    that a separate launch costs a + c and the fused one b."""
+    import torch
+
+    pkg = importlib.import_module("flashinfer-mlsys_b200")
+    wl = importlib.import_module("flashinfer-mlsys_b200.workloads")
+    dev = torch.device("cuda", 0)
+    Ts = tuple(int(t) for t in args.T.split(",")) if args.T else WORKLOADS["shared"][0]
+    w = wl.make_weights(32, 0, dev)
+    sh = tuple(t.to(dev) for t in wl.expert_weights(300, dev, 0))
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            flush.zero_()
+            fn()
+        evs = []
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        return statistics.mean(a.elapsed_time(b) for a, b in evs) * 1e3
+
+    sweep = {}
+    with ClockSampler(0) as clk:
+        for T in Ts:
+            a = wl.config_activations(T).to(dev)
+            none_bias = a.bias.float().clone()
+            none_bias[:32] -= 10.0  # no token picks a local expert
+            none_bias = none_bias.to(torch.bfloat16)
+            out = torch.empty((T, 7168), dtype=torch.bfloat16, device=dev)
+            routed = timed(lambda: pkg.kernel(a.logits, a.bias, a.hidden, a.hidden_scale, w.w13, w.s13, w.w2, w.s2,
+                                              0, 2.5, out))
+            fused = timed(lambda: pkg.kernel_shared(a.logits, a.bias, a.hidden, a.hidden_scale, w.w13, w.s13, w.w2,
+                                                    w.s2, 0, 2.5, *sh, out))
+            alone = timed(lambda: pkg.kernel_shared(a.logits, none_bias, a.hidden, a.hidden_scale, w.w13, w.s13,
+                                                    w.w2, w.s2, 0, 2.5, *sh, out))
+            sweep[str(T)] = {"routed_us": round(routed, 2), "fused_us": round(fused, 2),
+                             "shared_alone_us": round(alone, 2), "added_by_fusion_us": round(fused - routed, 2),
+                             "separate_total_us": round(routed + alone, 2)}
+    if pkg.device_status() != 0:
+        raise RuntimeError("device-side wait timed out during the benchmark")
+    line = {"metric": "us/call of the MoE layer with DeepSeek-V3's shared expert, fused vs separate",
+            "value": statistics.mean(v["fused_us"] for v in sweep.values()), "unit": "us/call (mean over T)",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+            "dtype": "e4m3 x e4m3 -> f32 (tcgen05 kind::f8f6f4)", "data": "synthetic, seeded",
+            "config": {"workload": f"shared: {WORKLOADS['shared'][1]}", "T": list(Ts), "l2": L2_NOTE},
+            "sweep": sweep, "gpu_launches": 4 * 3 * (args.steps + args.warmup) * len(Ts), "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -880,6 +942,8 @@ def main():
         bench_flashinfer(args)
     elif args.workload in ("quant", "addnorm"):
         bench_quant(args)
+    elif args.workload == "shared":
+        bench_shared(args)
     else:
         if args.workload is None:
             args.workload = "ep"

@@ -16,6 +16,7 @@ from .binding import (  # noqa: F401
     experts,
     kernel,
     kernel_ex,
+    kernel_shared,
     last_rows,
     quantize_activations,
     add_rmsnorm_quantize,
@@ -25,5 +26,5 @@ from . import workloads  # noqa: F401
 from ._lib import MoeError, lib_path, load  # noqa: F401
 
 __all__ = [
-    "kernel", "kernel_ex", "route", "experts", "quantize_activations", "add_rmsnorm_quantize", "device_status", "last_rows", "workloads", "MoeError", "load", "lib_path",
+    "kernel", "kernel_ex", "kernel_shared", "route", "experts", "quantize_activations", "add_rmsnorm_quantize", "device_status", "last_rows", "workloads", "MoeError", "load", "lib_path",
 ]

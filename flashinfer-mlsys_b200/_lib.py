@@ -21,6 +21,10 @@ SIGNATURES = {
         ctypes.c_int,
         [_vp] * 8 + [_c_int64, ctypes.c_double, _vp, _c_int64, _c_int64, _vp, _vp, _vp, _vp],
     ),
+    "moe_fp8_ds_kernel_shared": (
+        ctypes.c_int,
+        [_vp] * 8 + [_c_int64, ctypes.c_double] + [_vp] * 5 + [_c_int64, _c_int64, _vp],
+    ),
     "moe_fp8_ds_route": (ctypes.c_int, [_vp, _vp, _c_int64, _c_int64, _c_int64, ctypes.c_double, _vp, _vp, _vp, _vp]),
     "moe_fp8_ds_route_noalloc": (
         ctypes.c_int, [_vp, _vp, _c_int64, _c_int64, _c_int64, ctypes.c_double, _vp, _vp, _vp, _vp]),

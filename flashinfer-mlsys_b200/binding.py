@@ -165,6 +165,57 @@ def kernel(
 
 
 @torch.no_grad()
+def kernel_shared(
+    routing_logits: torch.Tensor,
+    routing_bias: torch.Tensor,
+    hidden_states: torch.Tensor,
+    hidden_states_scale: torch.Tensor,
+    gemm1_weights: torch.Tensor,
+    gemm1_weights_scale: torch.Tensor,
+    gemm2_weights: torch.Tensor,
+    gemm2_weights_scale: torch.Tensor,
+    local_expert_offset: int,
+    routed_scaling_factor: float,
+    shared_gemm1_weights: torch.Tensor,
+    shared_gemm1_weights_scale: torch.Tensor,
+    shared_gemm2_weights: torch.Tensor,
+    shared_gemm2_weights_scale: torch.Tensor,
+    output: torch.Tensor,
+) -> None:
+    """``kernel`` plus DeepSeek-V3's shared expert (weights of one expert:
+    e4m3 [4096, 7168] + f32 [32, 56], e4m3 [7168, 2048] + f32 [56, 16]) applied
+    to every token with weight 1 and added to the routed sum, in the same
+    launches (no counterpart in the reference's operator)."""
+    _need(routing_logits.dim() == 2, "routing_logits must be 2-D [seq_len, 256]")
+    T = routing_logits.shape[0]
+    e_local = gemm1_weights.shape[0]
+    dev = hidden_states.device
+    _need(dev.type == "cuda", "hidden_states must be a CUDA tensor")
+    _need(e_local in (32, 64, 128), "the shared expert needs 32, 64 or 128 local experts")
+    _chk(routing_logits, "routing_logits", torch.float32, (T, NUM_EXPERTS), dev)
+    _chk(routing_bias, "routing_bias", torch.bfloat16, (NUM_EXPERTS,), dev)
+    _chk(hidden_states, "hidden_states", _E4M3, (T, HIDDEN_SIZE), dev)
+    _chk(hidden_states_scale, "hidden_states_scale", torch.float32, (HIDDEN_SIZE // BLOCK_Q, T), dev)
+    _chk(output, "output", torch.bfloat16, (T, HIDDEN_SIZE), dev)
+    _weights_ok(gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, e_local, dev)
+    _chk(shared_gemm1_weights, "shared_gemm1_weights", _E4M3, (2 * INTERMEDIATE_SIZE, HIDDEN_SIZE), dev)
+    _chk(shared_gemm1_weights_scale, "shared_gemm1_weights_scale", torch.float32,
+         (2 * INTERMEDIATE_SIZE // BLOCK_Q, HIDDEN_SIZE // BLOCK_Q), dev)
+    _chk(shared_gemm2_weights, "shared_gemm2_weights", _E4M3, (HIDDEN_SIZE, INTERMEDIATE_SIZE), dev)
+    _chk(shared_gemm2_weights_scale, "shared_gemm2_weights_scale", torch.float32,
+         (HIDDEN_SIZE // BLOCK_Q, INTERMEDIATE_SIZE // BLOCK_Q), dev)
+    lib = _lib.load()
+    rc = _call(dev, lib.moe_fp8_ds_kernel_shared,
+               routing_logits.data_ptr(), routing_bias.data_ptr(), hidden_states.data_ptr(),
+               hidden_states_scale.data_ptr(), gemm1_weights.data_ptr(), gemm1_weights_scale.data_ptr(),
+               gemm2_weights.data_ptr(), gemm2_weights_scale.data_ptr(), int(local_expert_offset),
+               float(routed_scaling_factor), shared_gemm1_weights.data_ptr(), shared_gemm1_weights_scale.data_ptr(),
+               shared_gemm2_weights.data_ptr(), shared_gemm2_weights_scale.data_ptr(), output.data_ptr(), T,
+               e_local, _stream(dev))
+    _lib.check(rc, "moe_fp8_ds_kernel_shared")
+
+
+@torch.no_grad()
 def route(
     routing_logits: torch.Tensor,
     routing_bias: torch.Tensor,

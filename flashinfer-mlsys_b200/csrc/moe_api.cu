@@ -78,9 +78,12 @@ bool encode_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int64_t rows_cap_for(int64_t T, int e_local) {
+// Rows of the expert-major padded layout: every routed assignment, padding
+// of up to 127 rows per expert, and with a shared expert its T rows (+ padding).
+int64_t rows_cap_for(int64_t T, int e_local, bool shared = false) {
   const int64_t per_tok = e_local < kTopK ? e_local : kTopK;
-  return ((T * per_tok + kTileM - 1) / kTileM) * kTileM + (int64_t)e_local * kTileM;
+  return ((T * per_tok + kTileM - 1) / kTileM) * kTileM + (int64_t)e_local * kTileM +
+         (shared ? ((T + kTileM - 1) / kTileM) * kTileM : 0);
 }
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -88,8 +91,9 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // Computes the layout; when `base` is non-null also assigns the pointers.
 // `zero_bytes` receives the length of the prefix that must start zeroed
 // (self-resetting counters, the combine accumulator, split-K scratch).
-size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_bytes, bool routing_only = false) {
-  const int64_t rows = routing_only ? 0 : rows_cap_for(T, e_local);
+size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_bytes, bool routing_only = false,
+              bool shared = false) {
+  const int64_t rows = routing_only ? 0 : rows_cap_for(T, e_local, shared);
   size_t off = 0;
   auto take = [&](size_t bytes) {
     size_t o = off;
@@ -147,6 +151,7 @@ size_t layout(Workspace& w, int64_t T, int e_local, uint8_t* base, size_t* zero_
   w.rows_cap = rows;
   w.t_cap = T;
   w.e_local = e_local;
+  w.shared_cap = shared;
   return off;
 }
 
@@ -158,15 +163,17 @@ void forget_maps(const void* base, size_t bytes) {
   }
 }
 
-int get_workspace(int64_t T, int e_local, bool routing_only, Workspace** out) {
+int get_workspace(int64_t T, int e_local, bool routing_only, Workspace** out, bool shared = false) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MOE_ERR_CUDA;
   Workspace& w = g_ws[ws_key(dev, e_local, routing_only)];
-  if (w.base && w.t_cap >= T) {
+  if (w.base && w.t_cap >= T && (w.shared_cap || !shared)) {
     *out = &w;
     return MOE_OK;
   }
-  int64_t t_new = T;
+  // grow: keep the larger token capacity and any shared-expert capacity
+  const int64_t t_new = (w.base && w.t_cap > T) ? w.t_cap : T;
+  shared = shared || (w.base && w.shared_cap);
   if (w.base) {
     cudaDeviceSynchronize();
     forget_maps(w.base, w.bytes);
@@ -175,7 +182,7 @@ int get_workspace(int64_t T, int e_local, bool routing_only, Workspace** out) {
   }
   Workspace nw;
   size_t zero_bytes = 0;
-  const size_t bytes = layout(nw, t_new, e_local, nullptr, &zero_bytes, routing_only);
+  const size_t bytes = layout(nw, t_new, e_local, nullptr, &zero_bytes, routing_only, shared);
   void* base = nullptr;
   if (cudaMalloc(&base, bytes) != cudaSuccess) {
     cudaGetLastError();
@@ -185,7 +192,7 @@ int get_workspace(int64_t T, int e_local, bool routing_only, Workspace** out) {
     cudaFree(base);
     return MOE_ERR_CUDA;
   }
-  layout(nw, t_new, e_local, static_cast<uint8_t*>(base), nullptr, routing_only);
+  layout(nw, t_new, e_local, static_cast<uint8_t*>(base), nullptr, routing_only, shared);
   nw.base = base;
   nw.bytes = bytes;
   nw.zero_bytes = zero_bytes;
@@ -240,13 +247,23 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 bool valid_e_local(int64_t e) { return e == 32 || e == 64 || e == 128 || e == 256; }
 
-// The shared expert pipeline: plan (from logits or from given ids), permute,
-// both GEMMs and the finalize cast.
+// The common expert pipeline: plan (from logits or from given ids), permute,
+// both GEMMs and the finalize cast. sw1/ss1/sw2/ss2: an optional shared
+// expert (all four or none), scheduled as local expert E_l with every token.
 int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids, const float* given_w,
                  const void* hidden, const float* hidden_scale, const void* w1, const float* s1, const void* w2,
                  const float* s2, int64_t offset, double scale, void* out, int out_fp32, int64_t T, int64_t E_l,
-                 int32_t* user_ids, float* user_w, int32_t* user_counts, void* stream, bool route_only) {
+                 int32_t* user_ids, float* user_w, int32_t* user_counts, void* stream, bool route_only,
+                 const void* sw1 = nullptr, const float* ss1 = nullptr, const void* sw2 = nullptr,
+                 const float* ss2 = nullptr) {
   if (T < 0 || T > (int64_t(1) << 24) || !valid_e_local(E_l)) return MOE_ERR_INVALID_ARG;
+  const bool shared = sw1 != nullptr;
+  if (shared) {
+    if (!ss1 || !sw2 || !ss2 || E_l > 128) return MOE_ERR_INVALID_ARG;
+    if (!aligned16(sw1) || !aligned16(sw2)) return MOE_ERR_ALIGNMENT;
+  } else if (ss1 || sw2 || ss2) {
+    return MOE_ERR_INVALID_ARG;
+  }
   if (offset < -(int64_t(1) << 30) || offset > (int64_t(1) << 30)) return MOE_ERR_INVALID_ARG;
   if (T == 0) return check_device();  // empty tensors may carry null data pointers
   if (logits) {
@@ -265,10 +282,10 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
 
   std::lock_guard<std::mutex> lk(g_mu);
   Workspace* ws = nullptr;
-  rc = get_workspace(T, static_cast<int>(E_l), route_only, &ws);
+  rc = get_workspace(T, static_cast<int>(E_l), route_only, &ws, shared);
   if (rc) return rc;
 
-  if (logits && !route_only && !out_fp32 && T <= kDecMaxT && fused_decode_enabled()) {
+  if (logits && !route_only && !out_fp32 && !shared && T <= kDecMaxT && fused_decode_enabled()) {
     // one persistent kernel for routing, both GEMMs and the combine
     CUtensorMap mw1, mw2, mx1, mx2;
     if (!make_map(&mw1, w1, kHidden, static_cast<uint64_t>(E_l) * kGemm1N) ||
@@ -331,6 +348,11 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
       !make_map(&ma2, ws->inter, kInterCols, ws->rows_cap, a_box) ||
       !make_map(&mw2, w2, kInter, static_cast<uint64_t>(E_l) * kHidden))
     return MOE_ERR_CUDA;
+  // the shared expert's weights (one expert each); unused copies otherwise
+  CUtensorMap mws1 = mw1, mws2 = mw2;
+  if (shared && (!make_map(&mws1, sw1, kHidden, kGemm1N) || !make_map(&mws2, sw2, kInter, kHidden)))
+    return MOE_ERR_CUDA;
+  const int shared_e = shared ? static_cast<int>(E_l) : -1;
 
   PermuteArgs pa{};
   pa.hidden = static_cast<const uint8_t*>(hidden);
@@ -339,14 +361,16 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
   pa.offset = static_cast<int>(offset);
   pa.tokens_per_cta = ra.tokens_per_cta;
   pa.copy_rows = skinny ? 0 : 1;
+  pa.shared = shared ? 1 : 0;
   prof_mark(0, s);
   if (launch_route_permute(*ws, ra, pa, s) != cudaSuccess) return MOE_ERR_CUDA;
   prof_mark(1, s);
-  if (launch_gemm1(*ws, ma1, mw1, s1, s, skinny, hidden_scale, T) != cudaSuccess) return MOE_ERR_CUDA;
+  if (launch_gemm1(*ws, ma1, mw1, s1, s, skinny, hidden_scale, T, mws1, ss1, shared_e) != cudaSuccess)
+    return MOE_ERR_CUDA;
   prof_mark(2, s);
-  if (launch_gemm2(*ws, ma2, mw2, s2, s, skinny) != cudaSuccess) return MOE_ERR_CUDA;
+  if (launch_gemm2(*ws, ma2, mw2, s2, s, skinny, mws2, ss2, shared_e) != cudaSuccess) return MOE_ERR_CUDA;
   prof_mark(3, s);
-  if (launch_finalize(*ws, static_cast<int>(T), out, out_fp32, s) != cudaSuccess) return MOE_ERR_CUDA;
+  if (launch_finalize(*ws, static_cast<int>(T), out, out_fp32, s, shared_e) != cudaSuccess) return MOE_ERR_CUDA;
   prof_mark(4, s);
   g_prof_n = kProfKernels;
   g_prof_valid = g_prof_on;
@@ -380,6 +404,22 @@ int moe_fp8_ds_kernel(const float* routing_logits, const void* routing_bias, con
                               gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
                               routed_scaling_factor, output, seq_len, num_local_experts, nullptr, nullptr, nullptr,
                               stream);
+}
+
+int moe_fp8_ds_kernel_shared(const float* routing_logits, const void* routing_bias, const void* hidden_states,
+                             const float* hidden_states_scale, const void* gemm1_weights,
+                             const float* gemm1_weights_scale, const void* gemm2_weights,
+                             const float* gemm2_weights_scale, int64_t local_expert_offset,
+                             double routed_scaling_factor, const void* shared_gemm1_weights,
+                             const float* shared_gemm1_weights_scale, const void* shared_gemm2_weights,
+                             const float* shared_gemm2_weights_scale, void* output, int64_t seq_len,
+                             int64_t num_local_experts, void* stream) {
+  if (seq_len != 0 && (!routing_logits || !shared_gemm1_weights)) return MOE_ERR_INVALID_ARG;
+  return run_pipeline(routing_logits, routing_bias, nullptr, nullptr, hidden_states, hidden_states_scale,
+                      gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+                      routed_scaling_factor, output, 0, seq_len, num_local_experts, nullptr, nullptr, nullptr, stream,
+                      false, shared_gemm1_weights, shared_gemm1_weights_scale, shared_gemm2_weights,
+                      shared_gemm2_weights_scale);
 }
 
 int moe_fp8_ds_route(const float* routing_logits, const void* routing_bias, int64_t seq_len,

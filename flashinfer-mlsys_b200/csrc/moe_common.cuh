@@ -92,8 +92,8 @@ struct Plan {
   int split1;         // K split of GEMM1 (1 = no split)
   int split2;         // K split of GEMM2
   int n_assign;       // number of (token, local expert) pairs
-  int mtile_prefix[kExperts + 1];  // first m-tile of each local expert
-  int count[kExperts];             // rows (tokens) of each local expert
+  int mtile_prefix[kExperts + 2];  // first m-tile of each local expert (+ the shared expert, + the end)
+  int count[kExperts + 1];         // rows (tokens) of each local expert (+ the shared expert)
 };
 
 // Status word bits written by kernels (never trap).

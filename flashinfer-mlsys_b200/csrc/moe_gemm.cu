@@ -44,6 +44,8 @@ struct GemmArgs {
   const float* x_scale;
   int64_t x_ld;
   const float* w_scale;     // GEMM1: [E_l][32][56];  GEMM2: [E_l][56][16]
+  const float* ws_scale;    // the shared expert's scales ([32][56] / [56][16]) when shared_e >= 0
+  int shared_e;             // local expert index of the shared expert, or -1
   int rows_cap;
   int e_local;
   uint8_t* inter;           // GEMM1 out: [rows_cap][4096]
@@ -106,8 +108,8 @@ struct __align__(16) SmemCtl {
   int abort_flag;
   int plan_total;      // total m-tiles of the call
   int plan_split;      // K split of this GEMM
-  int prefix[kExperts + 1];
-  int count[kExperts];
+  int prefix[kExperts + 2];
+  int count[kExperts + 1];
   float amax[4][kTileM];
 };
 
@@ -273,6 +275,26 @@ __device__ __forceinline__ void fixup_quarter_g1(const GemmArgs& p, int gm, int 
   }
 }
 
+// The weight slabs of K block kb of unit x: GEMM1 128 gate rows + the matching
+// 128 up rows of W13[e]; GEMM2 256 rows of W2[e]. The shared expert (local
+// expert shared_e) is read through its own tensor map as expert 0.
+template <int kMode>
+__device__ __forceinline__ void load_weights(uint8_t* sb, const CUtensorMap* map_w, const CUtensorMap* map_ws,
+                                             const Unit& x, int kb, uint64_t* bar, int shared_e) {
+  const bool sh = x.e == shared_e;
+  const CUtensorMap* m = sh ? map_ws : map_w;
+  const int e = sh ? 0 : x.e;
+  if (kMode == 1) {
+    const int y0 = e * kGemm1N + x.n * kBlk;
+    tma_load_2d(sb, m, kb * kBlk, y0, bar);
+    tma_load_2d(sb + kStageA, m, kb * kBlk, y0 + kInter, bar);
+  } else {
+    const int y0 = e * kHidden + x.n * kTileN;
+    tma_load_2d(sb, m, kb * kBlk, y0, bar);
+    tma_load_2d(sb + kStageA, m, kb * kBlk, y0 + kBlk, bar);
+  }
+}
+
 // Bytes one pipeline stage receives: the two weight slabs plus the token
 // tile(s); GEMM1 of small calls gathers its rows in groups of four (the last
 // group repeats the unit's last row) instead of loading a 64-row box.
@@ -285,7 +307,7 @@ __device__ __forceinline__ uint32_t stage_tx_bytes(int rows) {
 template <int kMode, int kSkinny>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
-                    GemmArgs p) {
+                    const __grid_constant__ CUtensorMap map_ws, GemmArgs p) {
   using Cfg = GemmCfg<kMode, kSkinny>;
   static_assert(Cfg::kRing <= kRingBytes && Cfg::kStages <= kMaxStages, "stage ring does not fit");
   constexpr int NT = Cfg::kNT;
@@ -301,7 +323,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int E_l = p.e_local;
+  // local experts including a shared expert (the last one) when there is one
+  const int E_l = p.e_local + (p.shared_e >= 0 ? 1 : 0);
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -322,6 +345,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     fence_barrier_init();
     prefetch_tensormap(&map_a);
     prefetch_tensormap(&map_w);
+    if (p.shared_e >= 0) prefetch_tensormap(&map_ws);
   }
   if (warp == 1) {
     tmem_alloc(&ctl->tmem_base, 512);
@@ -353,15 +377,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int kb = x.kb0; kb < x.kb1 && n_pre < kStages; ++kb, ++n_pre) {
         uint8_t* sb = tiles + n_pre * kStageBytes + kBOff;
         mbar_arrive_expect_tx(&ctl->full[n_pre], stage_tx_bytes<kMode, kSkinny>(x.rows));
-        if (kMode == 1) {
-          const int y0 = x.e * kGemm1N + x.n * kBlk;
-          tma_load_2d(sb, &map_w, kb * kBlk, y0, &ctl->full[n_pre]);
-          tma_load_2d(sb + kStageA, &map_w, kb * kBlk, y0 + kInter, &ctl->full[n_pre]);
-        } else {
-          const int y0 = x.e * kHidden + x.n * kTileN;
-          tma_load_2d(sb, &map_w, kb * kBlk, y0, &ctl->full[n_pre]);
-          tma_load_2d(sb + kStageA, &map_w, kb * kBlk, y0 + kBlk, &ctl->full[n_pre]);
-        }
+        load_weights<kMode>(sb, &map_w, &map_ws, x, kb, &ctl->full[n_pre], p.shared_e);
       }
     }
   }
@@ -403,9 +419,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           ok = mbar_wait_bounded(&ctl->empty[s], ph ^ 1u, kWaitLimitNs);
           if (ok) {
             mbar_arrive_expect_tx(&ctl->full[s], stage_tx_bytes<kMode, kSkinny>(x.rows));
-            const int y0 = x.e * kGemm1N + x.n * kBlk;
-            tma_load_2d(sa + kBOff, &map_w, kb * kBlk, y0, &ctl->full[s]);
-            tma_load_2d(sa + kBOff + kStageA, &map_w, kb * kBlk, y0 + kInter, &ctl->full[s]);
+            load_weights<kMode>(sa + kBOff, &map_w, &map_ws, x, kb, &ctl->full[s], p.shared_e);
           }
         }
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -437,15 +451,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (static_cast<int>(it) >= n_pre) {
             if (!mbar_wait_bounded(&ctl->empty[s], ph ^ 1u, kWaitLimitNs)) { signal_abort(ctl, p.status); break; }
             mbar_arrive_expect_tx(&ctl->full[s], kStageBytes);
-            if (kMode == 1) {
-              const int y0 = x.e * kGemm1N + x.n * kBlk;
-              tma_load_2d(sb, &map_w, kb * kBlk, y0, &ctl->full[s]);
-              tma_load_2d(sb + kStageA, &map_w, kb * kBlk, y0 + kInter, &ctl->full[s]);
-            } else {
-              const int y0 = x.e * kHidden + x.n * kTileN;
-              tma_load_2d(sb, &map_w, kb * kBlk, y0, &ctl->full[s]);
-              tma_load_2d(sb + kStageA, &map_w, kb * kBlk, y0 + kBlk, &ctl->full[s]);
-            }
+            load_weights<kMode>(sb, &map_w, &map_ws, x, kb, &ctl->full[s], p.shared_e);
           }
           // token tile(s); the weights of a prefetched stage are already in flight
           tma_load_2d(sa, &map_a, kb * kBlk, x.gm * kTileM, &ctl->full[s]);
@@ -536,11 +542,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           cp_async_16(&sl->a[4 * lane], p.a_scale + (size_t)ka * p.rows_cap + (size_t)x.gm * kTileM + 4 * lane);
         }
         if (lane < 2) {
+          const bool sh = x.e == p.shared_e;
+          const float* wsc = sh ? p.ws_scale : p.w_scale;
+          const size_t e = sh ? 0 : x.e;
           const float* src;
           if (kMode == 1)
-            src = p.w_scale + ((size_t)x.e * kGemm1NBlocks + lane * kNT1 + x.n) * kHiddenBlocks + kb;
+            src = wsc + (e * kGemm1NBlocks + lane * kNT1 + x.n) * kHiddenBlocks + kb;
           else
-            src = p.w_scale + ((size_t)x.e * kHiddenBlocks + 2 * x.n + lane) * kInterBlocks + ka;
+            src = wsc + (e * kHiddenBlocks + 2 * x.n + lane) * kInterBlocks + ka;
           cp_async_4(&sl->w[lane], src);
         }
         cp_async_arrive_noinc(&ctl->sfull[j]);
@@ -702,8 +711,8 @@ size_t gemm_smem_bytes() { return kRingBytes + sizeof(SmemCtl) + 1024; }
 
 template <int kMode, int kSkinny>
 cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
-                        const float* w_scale, cudaStream_t s, int plan_early, const float* x_scale = nullptr,
-                        int64_t x_ld = 0) {
+                        const float* w_scale, cudaStream_t s, int plan_early, const CUtensorMap& map_ws,
+                        const float* ws_scale, int shared_e, const float* x_scale = nullptr, int64_t x_ld = 0) {
   // The shared-memory opt-in is a per-device function attribute: one bit per
   // device that has it (launches run under the library's host mutex).
   static uint64_t configured = 0;
@@ -723,6 +732,8 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
   p.plan = ws.plan;
   p.a_scale = (kMode == 1) ? ws.a1_scale : ws.inter_scale;
   p.w_scale = w_scale;
+  p.ws_scale = ws_scale;
+  p.shared_e = shared_e;
   p.rows_cap = static_cast<int>(ws.rows_cap);
   p.e_local = ws.e_local;
   p.inter = ws.inter;
@@ -738,7 +749,8 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
   p.tile_sem2 = ws.tile_sem2;
   p.status = ws.status;
   p.plan_early = plan_early;
-  return launch_k(moe_gemm_kernel<kMode, kSkinny>, dim3(sms), dim3(kGemmThreads), smem, s, true, map_a, map_w, p);
+  return launch_k(moe_gemm_kernel<kMode, kSkinny>, dim3(sms), dim3(kGemmThreads), smem, s, true, map_a, map_w,
+                  map_ws, p);
 }
 
 }  // namespace
@@ -748,15 +760,17 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
 // after that wait: the plan is complete when GEMM2 starts, and GEMM2 loads it
 // and issues its first weight tiles before waiting for GEMM1.
 cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
-                         const float* w_scale, cudaStream_t s, bool skinny, const float* x_scale, int64_t T) {
-  return skinny ? launch_gemm<1, 1>(ws, map_a, map_w, w_scale, s, 0, x_scale, T)
-                : launch_gemm<1, 0>(ws, map_a, map_w, w_scale, s, 0);
+                         const float* w_scale, cudaStream_t s, bool skinny, const float* x_scale, int64_t T,
+                         const CUtensorMap& map_ws, const float* ws_scale, int shared_e) {
+  return skinny ? launch_gemm<1, 1>(ws, map_a, map_w, w_scale, s, 0, map_ws, ws_scale, shared_e, x_scale, T)
+                : launch_gemm<1, 0>(ws, map_a, map_w, w_scale, s, 0, map_ws, ws_scale, shared_e);
 }
 
 cudaError_t launch_gemm2(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
-                         const float* w_scale, cudaStream_t s, bool skinny) {
-  return skinny ? launch_gemm<2, 1>(ws, map_a, map_w, w_scale, s, 1)
-                : launch_gemm<2, 0>(ws, map_a, map_w, w_scale, s, 1);
+                         const float* w_scale, cudaStream_t s, bool skinny, const CUtensorMap& map_ws,
+                         const float* ws_scale, int shared_e) {
+  return skinny ? launch_gemm<2, 1>(ws, map_a, map_w, w_scale, s, 1, map_ws, ws_scale, shared_e)
+                : launch_gemm<2, 0>(ws, map_a, map_w, w_scale, s, 1, map_ws, ws_scale, shared_e);
 }
 
 }  // namespace moe

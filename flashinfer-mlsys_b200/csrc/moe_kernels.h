@@ -75,6 +75,7 @@ struct Workspace {
   void* base = nullptr;            // single allocation backing everything above
   size_t bytes = 0;
   size_t zero_bytes = 0;           // length of the prefix that must be zero between calls
+  bool shared_cap = false;         // rows_cap includes a shared expert's T rows
 };
 
 struct RouteArgs {
@@ -104,6 +105,7 @@ struct PermuteArgs {
   int offset;
   int tokens_per_cta;
   int copy_rows;              // 0: record the row maps only (GEMM1 gathers the rows itself)
+  int shared;                 // 1: a shared expert is local expert e_local, every token's row t
 };
 
 // Launch `kernel` on `s`; with `pdl` the launch may overlap the tail of the
@@ -142,11 +144,16 @@ cudaError_t launch_route_permute(const Workspace& ws, const RouteArgs& a, const 
 // gathers its rows from hidden_states (map_a: hidden_states [T][7168] with
 // one-row boxes, x_scale its [56][T] scales); otherwise map_a is the permuted
 // rows with 128-row boxes. GEMM2's map_a has kSkinnyMaxRows-row boxes when skinny.
+// shared_e >= 0: local expert shared_e is a shared expert whose weights come
+// through map_ws / ws_scale (one expert); otherwise map_ws is unused.
 cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
-                         const float* w_scale, cudaStream_t s, bool skinny, const float* x_scale, int64_t T);
+                         const float* w_scale, cudaStream_t s, bool skinny, const float* x_scale, int64_t T,
+                         const CUtensorMap& map_ws, const float* ws_scale, int shared_e);
 cudaError_t launch_gemm2(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
-                         const float* w_scale, cudaStream_t s, bool skinny);
-cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32, cudaStream_t s);
+                         const float* w_scale, cudaStream_t s, bool skinny, const CUtensorMap& map_ws,
+                         const float* ws_scale, int shared_e);
+// shared_e >= 0: every token also adds its row of the shared expert (last)
+cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32, cudaStream_t s, int shared_e);
 
 // Expert-parallel token exchange (packed 7456-byte rows, see moe_ep.cu)
 cudaError_t launch_ep_pack(const void* hidden, const float* hidden_scale, const int32_t* ids, const float* w, int T,

@@ -30,10 +30,12 @@ constexpr uint64_t kRouteWaitLimitNs = 2000000000ull;  // 2 s: only reached if s
 // every local expert slot the token was routed to, and record the token's
 // rows. `prefix` is the m-tile prefix of the local experts, `base` the first
 // slot of the token's routing CTA inside every expert.
+// shared_row >= 0: the token's row of the shared expert (weight 1), which is
+// not listed in token_rows (the finalize adds it after the routed rows).
 __device__ __forceinline__ void permute_token(int t, int lane, const uint8_t* __restrict__ hidden,
                                               const float* __restrict__ hidden_scale, int T, int offset,
                                               const int* prefix, const int* base, const Workspace& ws,
-                                              bool copy_rows) {
+                                              bool copy_rows, int shared_row) {
   int row = -1;
   float w = 0.f;
   if (lane < kTopK) {
@@ -62,7 +64,7 @@ __device__ __forceinline__ void permute_token(int t, int lane, const uint8_t* __
       if (lane >= n_loc) ws.token_rows[(size_t)t * kTopK + lane] = -1;
     }
   }
-  const unsigned has = __ballot_sync(0xffffffffu, row >= 0);
+  const unsigned has = __ballot_sync(0xffffffffu, row >= 0) | (shared_row >= 0 ? (1u << 31) : 0u);
   if (!has) return;
   const uint4* src = reinterpret_cast<const uint4*>(hidden + (size_t)t * kHidden);
   const float sc0 = copy_rows ? __ldg(hidden_scale + (size_t)lane * T + t) : 0.f;
@@ -71,8 +73,8 @@ __device__ __forceinline__ void permute_token(int t, int lane, const uint8_t* __
   while (m) {
     const int k = __ffs(m) - 1;
     m &= m - 1;
-    const int r = __shfl_sync(0xffffffffu, row, k);
-    const float wk = __shfl_sync(0xffffffffu, w, k);
+    const int r = k == 31 ? shared_row : __shfl_sync(0xffffffffu, row, k);
+    const float wk = k == 31 ? 1.0f : __shfl_sync(0xffffffffu, w, k);
     if (copy_rows) {
       // 14 chunks of 16 B per lane; repeated destinations re-read the row from L1
       uint4* dst = reinterpret_cast<uint4*>(ws.a1 + (size_t)r * kHidden);
@@ -94,14 +96,14 @@ __device__ __forceinline__ void permute_token(int t, int lane, const uint8_t* __
 // of both GEMMs. With `write`, the plan and the optional user counts are
 // stored. Called by every thread of the CTA.
 __device__ __forceinline__ void build_plan(int c, int E_l, int* s_prefix, bool write, int32_t* user_counts,
-                                           const Workspace& ws) {
+                                           int n_user, const Workspace& ws) {
   __shared__ int warp_tot[2][kRouteThreads / 32];
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int nwarps = blockDim.x >> 5;
   if (write && tid < E_l) {
     ws.plan->count[tid] = c;
-    if (user_counts) user_counts[tid] = c;
+    if (user_counts && tid < n_user) user_counts[tid] = c;
   }
   const int m = (c + kTileM - 1) / kTileM;
   // block-wide exclusive scan of m-tiles and total of rows over the experts
@@ -223,7 +225,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
     __threadfence();
     if (tid < E_l) c = atomicExch(&ws.expert_fill[tid], 0);  // read and reset for the next call
   }
-  build_plan(c, E_l, s_prefix, true, a.user_counts, ws);
+  build_plan(c, E_l, s_prefix, true, a.user_counts, E_l, ws);
   if (tid == 0) *ws.done_ctas = 0u;
 }
 
@@ -239,11 +241,12 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
 __global__ void __launch_bounds__(kRouteThreads) route_permute_kernel(RouteArgs a, PermuteArgs pa, Workspace ws) {
   __shared__ int hist[kExperts];
   __shared__ int s_base[kExperts];
-  __shared__ int s_prefix[kExperts + 1];
+  __shared__ int s_prefix[kExperts + 2];
   __shared__ int s_ok;
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int E_l = a.e_local;
+  const int E_tot = E_l + (pa.shared ? 1 : 0);  // the shared expert, if any, is local expert E_l
   const int G = gridDim.x;
   // first kernel of a call: let GEMM1 get scheduled early (it runs its
   // prologue, then waits for this grid)
@@ -259,6 +262,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_permute_kernel(RouteArgs 
   if (G == 1) {
     for (int e = tid; e < E_l; e += blockDim.x) s_base[e] = 0;
     if (tid < E_l) c = hist[tid];
+    if (tid == E_l && pa.shared) c = a.T;
   } else {
     for (int e = tid; e < E_l; e += blockDim.x) {
       const int h = hist[e];
@@ -288,11 +292,13 @@ __global__ void __launch_bounds__(kRouteThreads) route_permute_kernel(RouteArgs 
     }
     __syncthreads();
     if (tid < E_l) c = __ldcg(&ws.expert_fill[tid]);
+    if (tid == E_l && pa.shared) c = a.T;
   }
-  build_plan(c, E_l, s_prefix, blockIdx.x == 0, a.user_counts, ws);
+  build_plan(c, E_tot, s_prefix, blockIdx.x == 0, a.user_counts, E_l, ws);
   if (s_ok) {
     for (int t = t_begin + warp; t < t_end; t += kRouteThreads / 32)
-      permute_token(t, lane, pa.hidden, pa.hidden_scale, pa.T, pa.offset, s_prefix, s_base, ws, pa.copy_rows != 0);
+      permute_token(t, lane, pa.hidden, pa.hidden_scale, pa.T, pa.offset, s_prefix, s_base, ws, pa.copy_rows != 0,
+                    pa.shared ? s_prefix[E_l] * kTileM + t : -1);
   } else {
     // the barrier gave up: no rows for these tokens (the finalize writes
     // zeros; the GEMMs only read rows inside the padded layout)
@@ -315,8 +321,11 @@ __global__ void __launch_bounds__(kRouteThreads) route_permute_kernel(RouteArgs 
 // cast once (ref_moe.py:166-167). Eight columns per thread.
 __global__ void __launch_bounds__(256) finalize_kernel(const __nv_bfloat16* __restrict__ rows_buf,
                                                        const int32_t* __restrict__ token_rows,
-                                                       void* __restrict__ out, int T, int out_fp32) {
+                                                       void* __restrict__ out, int T, int out_fp32,
+                                                       const Plan* __restrict__ plan, int shared_e) {
   griddep_wait();
+  // the shared expert's rows (one per token, in token order), added last
+  const int64_t shared_base = shared_e >= 0 ? (int64_t)plan->mtile_prefix[shared_e] * kTileM : -1;
   constexpr int kC8 = kHidden / 8;  // 896 eight-column chunks per token
   const int64_t n = (int64_t)T * kC8;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
@@ -331,6 +340,13 @@ __global__ void __launch_bounds__(256) finalize_kernel(const __nv_bfloat16* __re
       if (r[k] < 0) break;
       // 8 bf16 columns of the row; bf16 -> f32 is exact (upper half of the word)
       const uint4 q = __ldcs(reinterpret_cast<const uint4*>(rows_buf + (size_t)r[k] * kHidden) + c8);
+      s0.x += __uint_as_float(q.x << 16); s0.y += __uint_as_float(q.x & 0xFFFF0000u);
+      s0.z += __uint_as_float(q.y << 16); s0.w += __uint_as_float(q.y & 0xFFFF0000u);
+      s1.x += __uint_as_float(q.z << 16); s1.y += __uint_as_float(q.z & 0xFFFF0000u);
+      s1.z += __uint_as_float(q.w << 16); s1.w += __uint_as_float(q.w & 0xFFFF0000u);
+    }
+    if (shared_base >= 0) {
+      const uint4 q = __ldcs(reinterpret_cast<const uint4*>(rows_buf + (size_t)(shared_base + t) * kHidden) + c8);
       s0.x += __uint_as_float(q.x << 16); s0.y += __uint_as_float(q.x & 0xFFFF0000u);
       s0.z += __uint_as_float(q.y << 16); s0.w += __uint_as_float(q.y & 0xFFFF0000u);
       s1.x += __uint_as_float(q.z << 16); s1.y += __uint_as_float(q.z & 0xFFFF0000u);
@@ -427,14 +443,14 @@ cudaError_t launch_route_permute(const Workspace& ws, const RouteArgs& a, const 
   return cudaLaunchKernelEx(&cfg, route_permute_kernel, a, pa, ws);
 }
 
-cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32, cudaStream_t s) {
+cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32, cudaStream_t s, int shared_e) {
   const int64_t n8 = (int64_t)T * kHidden / 8;
   if (n8 == 0) return cudaSuccess;
   int64_t blocks = (n8 + 255) / 256;
   if (blocks > 16 * kSMs) blocks = 16 * kSMs;
   return launch_k(finalize_kernel, dim3((unsigned)blocks), dim3(256), 0, s, true,
                   static_cast<const __nv_bfloat16*>(ws.out_rows), static_cast<const int32_t*>(ws.token_rows), out, T,
-                  out_fp32);
+                  out_fp32, static_cast<const Plan*>(ws.plan), shared_e);
 }
 
 }  // namespace moe

@@ -85,6 +85,27 @@ int moe_fp8_ds_kernel_ex(const float* routing_logits, const void* routing_bias,
                          int32_t* expert_counts_out, void* stream);
 
 /*
+ * The layer with DeepSeek-V3's always-on shared expert fused in (no
+ * counterpart in the reference, whose operator has routed experts only; the
+ * shared expert follows DeepSeek-V3's MoE block: output = routed sum + shared
+ * expert of every token, weight 1). The shared expert has the routed experts'
+ * shapes and format: shared_gemm1_weights e4m3 [4096, 7168] with f32 scales
+ * [32, 56], shared_gemm2_weights e4m3 [7168, 2048] with f32 scales [56, 16].
+ * It is scheduled as one more local expert that every token uses, inside the
+ * same persistent GEMMs (no extra launch), and its row is added after the
+ * routed rows in the fp32 sum before the single bf16 cast. Other arguments as
+ * moe_fp8_ds_kernel; num_local_experts in {32, 64, 128}.
+ */
+int moe_fp8_ds_kernel_shared(const float* routing_logits, const void* routing_bias, const void* hidden_states,
+                             const float* hidden_states_scale, const void* gemm1_weights,
+                             const float* gemm1_weights_scale, const void* gemm2_weights,
+                             const float* gemm2_weights_scale, int64_t local_expert_offset,
+                             double routed_scaling_factor, const void* shared_gemm1_weights,
+                             const float* shared_gemm1_weights_scale, const void* shared_gemm2_weights,
+                             const float* shared_gemm2_weights_scale, void* output, int64_t seq_len,
+                             int64_t num_local_experts, void* stream);
+
+/*
  * Routing only: DeepSeek-V3 no-aux grouped top-k (ref_moe.py:95-126,
  * kernel.cu:157-198) plus the local per-expert histogram (kernel.cu:201-232).
  * Outputs as in moe_fp8_ds_kernel_ex; topk_ids_out and topk_weights_out are

@@ -140,13 +140,30 @@ def local_counts(topk_idx: np.ndarray, offset: int, e_local: int) -> np.ndarray:
     return np.bincount(le, minlength=e_local).astype(np.int64)
 
 
+def _expert_ffn(hidden_u8, hidden_scale, tok, w13, s13, w2, s2):
+    """One expert on tokens `tok` (ref_moe.py:148-162): dequantise, GEMM1,
+    SwiGLU (silu on the second half, the first half the multiplicand), GEMM2."""
+    A_e = dequant_rows(hidden_u8[tok], hidden_scale[:, tok])            # :69-78, :148
+    W13 = dequant_blocks(as_u8(w13), as_f32(s13))                       # :80-86
+    G1 = A_e @ W13.T                                                    # :153
+    X1, X2 = G1[:, :I], G1[:, I:]                                       # :156-157
+    C = (X2 / (np.float32(1.0) + np.exp(-X2))) * X1                     # :158-159
+    W2 = dequant_blocks(as_u8(w2), as_f32(s2))                          # :88-92
+    return C @ W2.T                                                     # :162
+
+
 def moe_forward(logits, bias, hidden_u8, hidden_scale, get_expert, offset: int, routed_scaling_factor: float,
-                e_local: int = 32, token_subset=None, routing=None):
+                e_local: int = 32, token_subset=None, routing=None, shared=None):
     """The whole layer (ref_moe.py:5-167) on CPU.
 
     get_expert(le) -> (w13_u8 [4096, 7168], s13 [32, 56], w2_u8 [7168, 2048], s2 [56, 16])
     token_subset: optional token indices; only those output rows are computed
     (each output row depends only on its own token).
+    shared: optional (w13, s13, w2, s2) of an always-on shared expert. The
+    reference's operator has none; this follows DeepSeek-V3's MoE block, whose
+    output is the routed sum plus the shared expert applied to every token with
+    weight 1. It is added to the fp32 accumulator after the routed experts,
+    before the single bf16 cast.
     Returns dict: out_f32 [n, 7168], out_bf16 (uint16 bits), rows, topk_idx, counts, routing.
     """
     r = routing if routing is not None else route(logits, bias, routed_scaling_factor)
@@ -165,17 +182,12 @@ def moe_forward(logits, bias, hidden_u8, hidden_scale, get_expert, offset: int, 
         if not sel.any():                                               # :141
             continue
         tok = rows[sel]                                                 # :144
-        w13, s13, w2, s2 = get_expert(le)
-        A_e = dequant_rows(hidden_u8[tok], hidden_scale[:, tok])        # :69-78, :148
-        W13 = dequant_blocks(as_u8(w13), as_f32(s13))                   # :80-86
-        G1 = A_e @ W13.T                                                # :153
-        X1, X2 = G1[:, :I], G1[:, I:]                                   # :156-157
-        C = (X2 / (np.float32(1.0) + np.exp(-X2))) * X1                 # :158-159
-        W2 = dequant_blocks(as_u8(w2), as_f32(s2))                      # :88-92
-        O = C @ W2.T                                                    # :162
+        O = _expert_ffn(hidden_u8, hidden_scale, tok, *get_expert(le))
         w_tok = weights[tok, ge]                                        # :165
         idx = np.fromiter((pos[int(t)] for t in tok), dtype=np.int64, count=len(tok))
         out[idx] += O * w_tok[:, None]                                  # :166
+    if shared is not None and len(rows):
+        out += _expert_ffn(hidden_u8, hidden_scale, rows, *shared)
     return {
         "out_f32": out, "out_bf16": f32_to_bf16_bits(out), "rows": rows, "topk_idx": topk_idx,
         "counts": local_counts(topk_idx, offset, e_local), "routing": r,
