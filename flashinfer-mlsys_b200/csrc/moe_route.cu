@@ -69,20 +69,38 @@ __device__ __forceinline__ void permute_token(int t, int lane, const uint8_t* __
   const uint4* src = reinterpret_cast<const uint4*>(hidden + (size_t)t * kHidden);
   const float sc0 = copy_rows ? __ldg(hidden_scale + (size_t)lane * T + t) : 0.f;
   const float sc1 = (copy_rows && lane + 32 < kHiddenBlocks) ? __ldg(hidden_scale + (size_t)(lane + 32) * T + t) : 0.f;
+  // the row in two halves of 7 chunks of 16 B per lane: each half is loaded
+  // once (its loads in flight together) and stored to every destination
+  constexpr int kChunks = kHidden / 16 / 32;  // 14
+  constexpr int kHalf = kChunks / 2;
+  for (int h = 0; h < 2; ++h) {
+    uint4 v[kHalf];
+    if (copy_rows) {
+#pragma unroll
+      for (int i = 0; i < kHalf; ++i) v[i] = __ldg(src + lane + 32 * (h * kHalf + i));
+    }
+    unsigned m = has;
+    while (m) {
+      const int k = __ffs(m) - 1;
+      m &= m - 1;
+      const int r = k == 31 ? shared_row : __shfl_sync(0xffffffffu, row, k);
+      if (copy_rows) {
+        uint4* dst = reinterpret_cast<uint4*>(ws.a1 + (size_t)r * kHidden);
+#pragma unroll
+        for (int i = 0; i < kHalf; ++i) dst[lane + 32 * (h * kHalf + i)] = v[i];
+        if (h == 0) {
+          ws.a1_scale[(size_t)lane * ws.rows_cap + r] = sc0;
+          if (lane + 32 < kHiddenBlocks) ws.a1_scale[(size_t)(lane + 32) * ws.rows_cap + r] = sc1;
+        }
+      }
+    }
+  }
   unsigned m = has;
   while (m) {
     const int k = __ffs(m) - 1;
     m &= m - 1;
     const int r = k == 31 ? shared_row : __shfl_sync(0xffffffffu, row, k);
     const float wk = k == 31 ? 1.0f : __shfl_sync(0xffffffffu, w, k);
-    if (copy_rows) {
-      // 14 chunks of 16 B per lane; repeated destinations re-read the row from L1
-      uint4* dst = reinterpret_cast<uint4*>(ws.a1 + (size_t)r * kHidden);
-#pragma unroll 7
-      for (int i = 0; i < kHidden / 16 / 32; ++i) dst[lane + 32 * i] = __ldg(src + lane + 32 * i);
-      ws.a1_scale[(size_t)lane * ws.rows_cap + r] = sc0;
-      if (lane + 32 < kHiddenBlocks) ws.a1_scale[(size_t)(lane + 32) * ws.rows_cap + r] = sc1;
-    }
     if (lane == 0) {
       ws.row_token[r] = t;
       ws.row_weight[r] = wk;
