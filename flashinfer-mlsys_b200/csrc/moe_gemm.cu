@@ -15,13 +15,9 @@
 // Warp roles (576 threads, one CTA per SM):
 //   warp 0      TMA producer (one elected lane): A tile 128x128 + two B slabs
 //               128x128 per K block into a 4-stage shared-memory ring.
-//   warp 1      TMEM owner + MMA issuer (one lane): per K block and per half
-//               of the N = 256 tile (GEMM1: gate | up; GEMM2: two 128-row W2
-//               slabs), 4 x tcgen05.mma (M128 N128 K32, e4m3 x e4m3 -> f32)
-//               into one of four 128-column TMEM partials (2 halves x 2
-//               buffers). The halves are released separately, so the next K
-//               block's first half can start while the epilogue still reads
-//               the second.
+//   warp 1      TMEM owner + MMA issuer (one lane): 4 x tcgen05.mma
+//               (M128 N256 K32, e4m3 x e4m3 -> f32) per K block into one of
+//               two 256-column TMEM partial accumulators.
 //   warp 2      scale loader: cp.async copies of the 128 row scales and the
 //               weight-block scales of every K block into an 8-deep shared
 //               ring, running ahead of the epilogue.
@@ -104,8 +100,8 @@ struct __align__(16) SmemCtl {
   uint64_t sempty[kScaleSlots];
   uint64_t full[kMaxStages];
   uint64_t empty[kMaxStages];
-  uint64_t tfull[2][2];   // [half][buffer]: the MMAs of that partial are done
-  uint64_t tempty[2][2];  // [half][buffer]: the epilogue has read that partial
+  uint64_t tfull[2];
+  uint64_t tempty[2];
   uint64_t mma_done;
   uint64_t epi_bar;   // barrier among the 16 epilogue warps (bounded waits)
   uint32_t tmem_base;
@@ -336,12 +332,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&ctl->empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
-      for (int h = 0; h < 2; ++h) {
-        mbar_init(&ctl->tfull[h][b], 1);
-        // GEMM1: every epilogue warp reads both halves (gate and up columns);
-        // GEMM2: a warp's 64 columns lie in one half
-        mbar_init(&ctl->tempty[h][b], kMode == 1 ? kEpiWarps : kEpiWarps / 2);
-      }
+      mbar_init(&ctl->tfull[b], 1);
+      mbar_init(&ctl->tempty[b], kEpiWarps);
     }
     for (int j = 0; j < kScaleSlots; ++j) {
       mbar_init(&ctl->sfull[j], 32);
@@ -477,15 +469,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ======================= MMA issuer =======================
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_e4m3_f32(kTileM, kTileN / 2);
+      constexpr uint32_t idesc = idesc_e4m3_f32(kTileM, kTileN);
       uint32_t it = 0, gkb = 0;
       bool issued_any = false;
       for (int u = blockIdx.x; u < units && !aborted(ctl); u += gridDim.x) {
         const Unit x = decode_unit<kMode>(u, split, ctl->prefix, ctl->count, E_l);
         for (int kb = x.kb0; kb < x.kb1; ++kb, ++it, ++gkb) {
           const uint32_t buf = gkb & 1u;
-          const uint32_t tph = ((gkb >> 1) & 1u) ^ 1u;
-          if (!mbar_wait_bounded(&ctl->tempty[0][buf], tph, kWaitLimitNs)) {
+          if (!mbar_wait_bounded(&ctl->tempty[buf], ((gkb >> 1) & 1u) ^ 1u, kWaitLimitNs)) {
             signal_abort(ctl, p.status);
             break;
           }
@@ -497,36 +488,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tc_fence_after();
           const uint32_t sa = smem_u32(tiles + s * kStageBytes);
           const uint32_t sb = sa + kBOff;
-          bool half_ok = true;
+          const uint64_t db = smem_desc_sw128(sb);
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            if (h == 1) {
-              if (!mbar_wait_bounded(&ctl->tempty[1][buf], tph, kWaitLimitNs)) {
-                half_ok = false;
-                break;
-              }
-              tc_fence_after();
+          for (int a = 0; a < Cfg::kATiles; ++a) {
+            const uint64_t da = smem_desc_sw128(sa + a * kABytes);
+#pragma unroll
+            for (int k = 0; k < kBlk / 32; ++k) {
+              // advance 32 bytes (one K=32 slice) inside the swizzle atom
+              mma_f8f6f4(tmem + buf * kTileN, da + 2 * k, db + 2 * k, idesc, (a > 0 || k > 0) ? 1u : 0u);
             }
-            // B slab h: rows [128h, 128h + 128) of the stage's 256-row tile
-            const uint64_t db = smem_desc_sw128(sb + h * kStageA);
-            const uint32_t d = tmem + (buf * 2 + h) * (kTileN / 2);
-#pragma unroll
-            for (int a = 0; a < Cfg::kATiles; ++a) {
-              const uint64_t da = smem_desc_sw128(sa + a * kABytes);
-#pragma unroll
-              for (int k = 0; k < kBlk / 32; ++k) {
-                // advance 32 bytes (one K=32 slice) inside the swizzle atom
-                mma_f8f6f4(d, da + 2 * k, db + 2 * k, idesc, (a > 0 || k > 0) ? 1u : 0u);
-              }
-            }
-            issued_any = true;
-            mma_commit(&ctl->tfull[h][buf]);
           }
-          if (!half_ok) {
-            signal_abort(ctl, p.status);
-            break;
-          }
+          issued_any = true;
           mma_commit(&ctl->empty[s]);
+          mma_commit(&ctl->tfull[buf]);
         }
         if (aborted(ctl)) break;
       }
@@ -621,42 +595,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl->sempty[j]);
-        // columns of this warp: GEMM1 gate [32cg, 32cg+32) in half 0 and the
-        // matching up columns in half 1; GEMM2 [64cg, 64cg+64), all in half cg/2
-#pragma unroll
-        for (int hh = 0; hh < (kMode == 1 ? 2 : 1); ++hh) {
-          const int h = (kMode == 1) ? hh : (cg >> 1);
-          const bool got =
-              __all_sync(0xffffffffu, mbar_wait_bounded(&ctl->tfull[h][buf], (gkb >> 1) & 1u, kWaitLimitNs));
-          if (!got) {
-            signal_abort(ctl, p.status);
-            ok = false;
-            break;
-          }
-          __syncwarp();
-          tc_fence_after();
-          const uint32_t tb = t_lane + (buf * 2 + h) * (kTileN / 2) + ((kMode == 1) ? cg * 32 : (cg & 1) * 64);
-          if (kMode == 1) {
-            const float f = hh == 0 ? f0 : f1;
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              float v[16];
-              tmem_ld_32x32b_x16(tb + 16 * i, v);
-              promote16(acc + 32 * hh + 16 * i, v, f);
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              float v[16];
-              tmem_ld_32x32b_x16(tb + 16 * i, v);
-              promote16(acc + 16 * i, v, f0);
-            }
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&ctl->tempty[h][buf]);
+        const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(&ctl->tfull[buf], (gkb >> 1) & 1u, kWaitLimitNs));
+        if (!got) {
+          signal_abort(ctl, p.status);
+          ok = false;
+          break;
         }
-        if (!ok) break;
+        __syncwarp();
+        tc_fence_after();
+        const uint32_t tb = t_lane + buf * kTileN;
+        // columns of this warp: GEMM1 gate [32cg, 32cg+32) and up [128+32cg, ...);
+        // GEMM2 [64cg, 64cg+64)
+        const uint32_t c0 = (kMode == 1) ? cg * 32 : cg * 64;
+        const uint32_t c1 = (kMode == 1) ? kBlk + cg * 32 : cg * 64 + 32;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          float v[16];
+          const uint32_t col = (h < 2) ? c0 + 16 * h : c1 + 16 * (h - 2);
+          const float f = (h < 2) ? f0 : f1;
+          tmem_ld_32x32b_x16(tb + col, v);
+          promote16(acc + 16 * h, v, f);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->tempty[buf]);
       }
       if (!ok) break;
 
