@@ -269,19 +269,22 @@ def _roofline_gemm1(stats, g1_ms, hbm_peak, peak_src, fp8, fp8_2x_sustained, tra
     flops = sum(_gemm1_flops(s["n_assign"]) for s in stats)
     if g1_ms <= 0:
         return None
+    traffic = _ncu_traffic(traffic_key, byts / max(1, len(stats)))
     fp8_nominal = 2 * _peaks()[1]
     if flops / (fp8_nominal * 1e12) > byts / (hbm_peak * 1e9):
         peak, src = fp8.get()
         ach = flops / (g1_ms * 1e-3) / 1e12
         return {"bound": "tensor", "kernel": "moe_gemm_kernel<1> (GEMM1 + SwiGLU + requant)", "achieved": round(ach, 1),
                 "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(ach / peak, 4), "peak_source": src,
-                "frac_of_2x_bf16_sustained": round(ach / fp8_2x_sustained, 4), "traffic": None,
+                "frac_of_2x_bf16_sustained": round(ach / fp8_2x_sustained, 4),
+                "traffic": traffic["bytes"] if traffic else None, "traffic_detail": traffic,
                 "algorithmic_flops": flops}
     ach = byts / (g1_ms * 1e-3) / 1e9
     return {"bound": "hbm", "kernel": "moe_gemm_kernel<1> (GEMM1 + SwiGLU + requant)", "achieved": round(ach, 1),
             "peak": hbm_peak, "unit": "GB/s", "frac": round(ach / hbm_peak, 4),
             "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src,
-            "traffic": _ncu_traffic(traffic_key), "algorithmic_bytes": byts}
+            "traffic": traffic["bytes"] if traffic else None, "traffic_detail": traffic,
+            "algorithmic_bytes_per_launch": int(byts / max(1, len(stats)))}
 
 
 def _measure_layer(pkg, lib, dev, stream, flush, w, acts_cpu, e_local, steps, warmup, kernels=True, e2e=True):
@@ -438,16 +441,22 @@ def _sustained_bf16():
     return 1400.0
 
 
-def _ncu_traffic(key):
-    """DRAM bytes per launch of a kernel from a committed ncu summary (ncu
-    cannot run inside the benchmark); None when there is none."""
+def _ncu_traffic(key, algorithmic_per_launch):
+    """DRAM bytes per launch of GEMM1 for this run's calls, from the committed
+    ncu capture of the same workload (ncu cannot run inside the benchmark):
+    the capture's DRAM/algorithmic ratio times this run's algorithmic bytes
+    per launch (exact where the capture covered the same calls). None when
+    there is no capture."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(p):
-        try:
-            return json.load(open(p)).get(key)
-        except (OSError, ValueError):
-            return None
-    return None
+    try:
+        d = json.load(open(p)).get(key)
+    except (OSError, ValueError):
+        return None
+    if not isinstance(d, dict) or not d.get("algorithmic_bytes"):
+        return None
+    ratio = d["dram_bytes"] / d["algorithmic_bytes"]
+    return {"bytes": int(ratio * algorithmic_per_launch), "ratio_to_algorithmic": round(ratio, 3),
+            "source": f"profiles/traffic.json[{key}]: {d.get('case')}"}
 
 
 # ---------------------------------------------------------------------------
