@@ -368,7 +368,7 @@ int run_pipeline(const float* logits, const void* bias, const int32_t* given_ids
   if (launch_gemm1(*ws, ma1, mw1, s1, s, skinny, hidden_scale, T, mws1, ss1, shared_e) != cudaSuccess)
     return MOE_ERR_CUDA;
   prof_mark(2, s);
-  if (launch_gemm2(*ws, ma2, mw2, s2, s, skinny, mws2, ss2, shared_e) != cudaSuccess) return MOE_ERR_CUDA;
+  if (launch_gemm2(*ws, ma2, mw2, s2, s, skinny, mws2, ss2, shared_e, static_cast<int>(T)) != cudaSuccess) return MOE_ERR_CUDA;
   prof_mark(3, s);
   if (launch_finalize(*ws, static_cast<int>(T), out, out_fp32, s, shared_e) != cudaSuccess) return MOE_ERR_CUDA;
   prof_mark(4, s);

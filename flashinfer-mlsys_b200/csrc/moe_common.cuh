@@ -81,6 +81,15 @@ constexpr int kScaleSlots = 8;                // depth of the scale ring (K bloc
 
 // Split-K of GEMM1 reduces fp32 partial tiles in a bounded scratch area.
 constexpr int kMaxSplitMTiles = 32;
+// Calls of at most kSkinnyMaxRows tokens, and calls of at most kDirectMaxT
+// tokens whose GEMM2 is split along K, combine directly: every GEMM2 partial
+// adds its routing-weighted product into a per-token fp32 sum (GEMM2's split-K
+// scratch, [kDirectMaxT][7168]), which the finalize kernel casts to the output
+// and clears.
+constexpr int kDirectMaxT = kMaxSplitMTiles * 128;
+__host__ __device__ __forceinline__ bool direct_combine(int split2, int T) {
+  return T <= kSkinnyMaxRows || (split2 > 1 && T <= kDirectMaxT);
+}
 
 constexpr int kSMs = 148;
 

@@ -10,7 +10,11 @@
 //     per block the hi and lo tiles are both multiplied against the same W2
 //     tile into one TMEM partial (they share the scale s), then
 //     out_rows[r, :] = bf16(routing_weight(r) * O[r, :])  (ref_moe.py:162-166;
-//     the combine sums these rows in fp32).
+//     the combine sums these rows in fp32). Direct-combine calls (small or
+//     split-K ones, see direct_combine) instead add routing_weight(r) *
+//     O[r, :] into their token's fp32 sum, cast once by the finalize kernel;
+//     with 64-row tiles their hi and lo tiles form one 128-row operand: one
+//     MMA per K slice puts hi x W in TMEM lanes 0-63 and lo x W in 64-127.
 //
 // Warp roles (576 threads, one CTA per SM):
 //   warp 0      TMA producer (one elected lane): A tile 128x128 + two B slabs
@@ -56,6 +60,7 @@ struct GemmArgs {
   __nv_bfloat16* out_rows;  // GEMM2 out: [rows_cap][7168] weighted expert outputs (bf16)
   float* g2_part;           // GEMM2 split-K scratch: [kMaxSplitMTiles*128][7168]
   int32_t* tile_sem2;       // GEMM2 split-K counters: [kMaxSplitMTiles][28][16 epilogue warps]
+  int T;                    // tokens of the call (GEMM2: direct combine, see direct_combine)
   unsigned* status;
   int plan_early;           // 1: the plan was complete before the previous kernel released this one
 };
@@ -391,6 +396,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int total_mtiles = ctl->plan_total;
   const int split = ctl->plan_split;
+  // GEMM2 of a direct-combine call (direct_combine) adds its partials into
+  // per-token sums; with 64-row tiles its hi and lo rows share one M=128 MMA
+  // (their products land in different TMEM lanes and meet in those sums).
+  const bool direct = (kMode == 2) && direct_combine(split, p.T);
+  const bool stacked = (kMode == 2 && kSkinny == 1 && direct);
   const int units = total_mtiles * NT * split;
   const uint32_t tmem = ctl->tmem_base;
 
@@ -470,6 +480,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ======================= MMA issuer =======================
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_e4m3_f32(kTileM, kTileN);
+      // stacked GEMM2: the 64-row hi and lo tiles are adjacent in the stage,
+      // i.e. one 128-row operand; a single MMA per K slice gives hi x W in
+      // TMEM lanes 0-63 and lo x W in lanes 64-127
+      const int n_atiles = stacked ? 1 : Cfg::kATiles;
       uint32_t it = 0, gkb = 0;
       bool issued_any = false;
       for (int u = blockIdx.x; u < units && !aborted(ctl); u += gridDim.x) {
@@ -491,6 +505,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint64_t db = smem_desc_sw128(sb);
 #pragma unroll
           for (int a = 0; a < Cfg::kATiles; ++a) {
+            if (a >= n_atiles) break;
             const uint64_t da = smem_desc_sw128(sa + a * kABytes);
 #pragma unroll
             for (int k = 0; k < kBlk / 32; ++k) {
@@ -537,7 +552,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // hidden_states_scale [56][T]: block kb of each gathered token
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            if (y[i] >= 0) cp_async_4(&sl->a[4 * lane + i], p.x_scale + (size_t)kb * p.x_ld + y[i]);
+            if (static_cast<uint64_t>(y[i]) < static_cast<uint64_t>(p.x_ld))
+              cp_async_4(&sl->a[4 * lane + i], p.x_scale + (size_t)kb * p.x_ld + y[i]);
         } else {
           cp_async_16(&sl->a[4 * lane], p.a_scale + (size_t)ka * p.rows_cap + (size_t)x.gm * kTileM + 4 * lane);
         }
@@ -561,7 +577,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ======================= epilogue (16 warps) =======================
     const int q = warp & 3;              // TMEM lane quarter accessible to this warp
     const int cg = (warp - kEpiWarp0) >> 2;  // column group 0..3
-    const int row_in_tile = q * 32 + lane;
+    // padded row of this thread's TMEM lane (stacked GEMM2: lanes 64-127 hold
+    // the lo products of rows 0-63)
+    const int row_in_tile = stacked ? ((q & 1) * 32 + lane) : q * 32 + lane;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(q * 32) << 16);
     uint32_t gkb = 0;
     EpiSync es;
@@ -655,7 +673,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       } else {
         const float w = valid ? __ldg(p.row_weight + row) : 0.f;
         __nv_bfloat16* dst = p.out_rows + row * kHidden + x.n * kTileN + cg * 64;
-        if (split == 1) {
+        if (direct) {
+          // direct combine: the weighted partial goes straight into its
+          // token's fp32 sum; no arrival counting (the finalize kernel, which
+          // runs after this grid completes, casts the sums)
+          // (a row's token is checked: after a routing timeout its slot may be stale)
+          const int tok = valid ? __ldg(p.row_token + row) : -1;
+          if (static_cast<unsigned>(tok) < static_cast<unsigned>(p.T)) {
+            float* g = p.g2_part + (size_t)tok * kHidden + x.n * kTileN + cg * 64;
+#pragma unroll
+            for (int i = 0; i < 64; i += 4)
+              red_add_v4(g + i, w * acc[i], w * acc[i + 1], w * acc[i + 2], w * acc[i + 3]);
+          }
+        } else if (split == 1) {
           if (valid) {
 #pragma unroll
             for (int i = 0; i < 64; i += 16) store_bf16x16(dst + i, w, acc + i);
@@ -712,7 +742,8 @@ size_t gemm_smem_bytes() { return kRingBytes + sizeof(SmemCtl) + 1024; }
 template <int kMode, int kSkinny>
 cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
                         const float* w_scale, cudaStream_t s, int plan_early, const CUtensorMap& map_ws,
-                        const float* ws_scale, int shared_e, const float* x_scale = nullptr, int64_t x_ld = 0) {
+                        const float* ws_scale, int shared_e, const float* x_scale = nullptr, int64_t x_ld = 0,
+                        int T = 0) {
   // The shared-memory opt-in is a per-device function attribute: one bit per
   // device that has it (launches run under the library's host mutex).
   static uint64_t configured = 0;
@@ -749,6 +780,7 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
   p.tile_sem2 = ws.tile_sem2;
   p.status = ws.status;
   p.plan_early = plan_early;
+  p.T = T;
   return launch_k(moe_gemm_kernel<kMode, kSkinny>, dim3(sms), dim3(kGemmThreads), smem, s, true, map_a, map_w,
                   map_ws, p);
 }
@@ -768,9 +800,9 @@ cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CU
 
 cudaError_t launch_gemm2(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
                          const float* w_scale, cudaStream_t s, bool skinny, const CUtensorMap& map_ws,
-                         const float* ws_scale, int shared_e) {
-  return skinny ? launch_gemm<2, 1>(ws, map_a, map_w, w_scale, s, 1, map_ws, ws_scale, shared_e)
-                : launch_gemm<2, 0>(ws, map_a, map_w, w_scale, s, 1, map_ws, ws_scale, shared_e);
+                         const float* ws_scale, int shared_e, int T) {
+  return skinny ? launch_gemm<2, 1>(ws, map_a, map_w, w_scale, s, 1, map_ws, ws_scale, shared_e, nullptr, 0, T)
+                : launch_gemm<2, 0>(ws, map_a, map_w, w_scale, s, 1, map_ws, ws_scale, shared_e, nullptr, 0, T);
 }
 
 }  // namespace moe

@@ -66,7 +66,7 @@ struct Workspace {
   float* inter_scale = nullptr;    // [16][rows_cap] hi scales (lo = hi / 16)
   float* g_part = nullptr;         // [kMaxSplitMTiles*128][4096] GEMM1 split-K partial sums (kept zero)
   int32_t* tile_sem = nullptr;     // [kMaxSplitMTiles][16][4] GEMM1 split-K arrival counters (kept zero)
-  float* g2_part = nullptr;        // [kMaxSplitMTiles*128][7168] GEMM2 split-K partial sums (kept zero)
+  float* g2_part = nullptr;        // [kMaxSplitMTiles*128][7168] GEMM2 split-K partial sums by row, or by token in a direct-combine call (kept zero)
   int32_t* tile_sem2 = nullptr;    // [kMaxSplitMTiles][28][16] GEMM2 split-K arrival counters (kept zero)
   __nv_bfloat16* out_rows = nullptr;  // [rows_cap][7168] routing-weighted expert output of every permuted row (bf16)
   int32_t* token_rows = nullptr;   // [t_cap][8] permuted rows of each token, ascending expert id, -1 padded
@@ -151,8 +151,9 @@ cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CU
                          const CUtensorMap& map_ws, const float* ws_scale, int shared_e);
 cudaError_t launch_gemm2(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
                          const float* w_scale, cudaStream_t s, bool skinny, const CUtensorMap& map_ws,
-                         const float* ws_scale, int shared_e);
-// shared_e >= 0: every token also adds its row of the shared expert (last)
+                         const float* ws_scale, int shared_e, int T);
+// shared_e >= 0: every token also adds its row of the shared expert (last);
+// a direct-combine call (direct_combine) casts the per-token sums instead
 cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32, cudaStream_t s, int shared_e);
 
 // Expert-parallel token exchange (packed 7456-byte rows, see moe_ep.cu)

@@ -24,6 +24,13 @@ constexpr int kMinTokensPerCta = 8;
 #define MOE_SPLIT_UNIT_OVERHEAD 16
 #endif
 constexpr int kSplitUnitOverhead = MOE_SPLIT_UNIT_OVERHEAD;
+// The same for GEMM2 of a call of at most 64 tokens: its partials add into
+// per-token sums (no arrival counting, no read-back), so a unit costs little
+// beyond its K blocks.
+#ifndef MOE_DIRECT_UNIT_OVERHEAD
+#define MOE_DIRECT_UNIT_OVERHEAD 2
+#endif
+constexpr int kDirectUnitOverhead = MOE_DIRECT_UNIT_OVERHEAD;
 constexpr uint64_t kRouteWaitLimitNs = 2000000000ull;  // 2 s: only reached if something is broken
 
 // One warp, one token: copy the e4m3 row (7168 B) and its 56 block scales to
@@ -111,10 +118,10 @@ __device__ __forceinline__ void permute_token(int t, int lane, const uint8_t* __
 // The device-side plan from the per-expert counts (thread e < E_l holds the
 // count `c` of local expert e): m-tile prefix (also left in `s_prefix`,
 // E_l + 1 entries), the number of (token, local expert) pairs and the K split
-// of both GEMMs. With `write`, the plan and the optional user counts are
-// stored. Called by every thread of the CTA.
+// of both GEMMs for a call of T tokens. With `write`, the plan and the
+// optional user counts are stored. Called by every thread of the CTA.
 __device__ __forceinline__ void build_plan(int c, int E_l, int* s_prefix, bool write, int32_t* user_counts,
-                                           int n_user, const Workspace& ws) {
+                                           int n_user, const Workspace& ws, int T) {
   __shared__ int warp_tot[2][kRouteThreads / 32];
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -148,14 +155,17 @@ __device__ __forceinline__ void build_plan(int c, int E_l, int* s_prefix, bool w
   if (tid == 0) s_prefix[E_l] = total;
   if (write && warp == 0) {
     // K split: minimise waves * (K blocks per unit + per-unit overhead); lane = split - 1
-    auto cost = [&](int tiles, int nkb, int smax, int sp) -> long long {
+    auto cost = [&](int tiles, int nkb, int smax, int sp, int overhead) -> long long {
       if (sp > smax || tiles <= 0) return 0x7fffffffffffLL;
       const long long units = (long long)tiles * sp;
-      return ((units + kSMs - 1) / kSMs) * ((nkb + sp - 1) / sp + kSplitUnitOverhead);
+      return ((units + kSMs - 1) / kSMs) * ((nkb + sp - 1) / sp + overhead);
     };
     const int sp = lane + 1;
-    const long long c1 = (total <= kMaxSplitMTiles) ? cost(total * kNT1, kKB1, 14, sp) : (sp == 1 ? 0 : 0x7fffffffffffLL);
-    const long long c2 = (total <= kMaxSplitMTiles) ? cost(total * kNT2, kKB2, 4, sp) : (sp == 1 ? 0 : 0x7fffffffffffLL);
+    const int oh2 = T <= kSkinnyMaxRows ? kDirectUnitOverhead : kSplitUnitOverhead;
+    const long long c1 =
+        (total <= kMaxSplitMTiles) ? cost(total * kNT1, kKB1, 14, sp, kSplitUnitOverhead) : (sp == 1 ? 0 : 0x7fffffffffffLL);
+    const long long c2 =
+        (total <= kMaxSplitMTiles) ? cost(total * kNT2, kKB2, 4, sp, oh2) : (sp == 1 ? 0 : 0x7fffffffffffLL);
     // pack (cost, split) so that the minimum prefers the smaller split on ties
     unsigned long long k1 = (static_cast<unsigned long long>(c1) << 8) | sp;
     unsigned long long k2 = (static_cast<unsigned long long>(c2) << 8) | sp;
@@ -214,7 +224,6 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
   __shared__ int s_prefix[kExperts + 1];
   __shared__ int is_last;
   const int tid = threadIdx.x;
-  const int warp = tid >> 5, lane = tid & 31;
   const int E_l = a.e_local;
   for (int e = tid; e < E_l; e += blockDim.x) hist[e] = 0;
   __syncthreads();
@@ -243,7 +252,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_plan_kernel(RouteArgs a, 
     __threadfence();
     if (tid < E_l) c = atomicExch(&ws.expert_fill[tid], 0);  // read and reset for the next call
   }
-  build_plan(c, E_l, s_prefix, true, a.user_counts, E_l, ws);
+  build_plan(c, E_l, s_prefix, true, a.user_counts, E_l, ws, a.T);
   if (tid == 0) *ws.done_ctas = 0u;
 }
 
@@ -312,7 +321,9 @@ __global__ void __launch_bounds__(kRouteThreads) route_permute_kernel(RouteArgs 
     if (tid < E_l) c = __ldcg(&ws.expert_fill[tid]);
     if (tid == E_l && pa.shared) c = a.T;
   }
-  build_plan(c, E_tot, s_prefix, blockIdx.x == 0, a.user_counts, E_l, ws);
+  // a CTA whose barrier wait gave up plans nothing (CTA 0's plan is the
+  // GEMMs': an empty plan launches no work on rows that were never written)
+  build_plan(s_ok ? c : 0, E_tot, s_prefix, blockIdx.x == 0, a.user_counts, E_l, ws, a.T);
   if (s_ok) {
     for (int t = t_begin + warp; t < t_end; t += kRouteThreads / 32)
       permute_token(t, lane, pa.hidden, pa.hidden_scale, pa.T, pa.offset, s_prefix, s_base, ws, pa.copy_rows != 0,
@@ -336,39 +347,52 @@ __global__ void __launch_bounds__(kRouteThreads) route_permute_kernel(RouteArgs 
 
 // out[t, :] = sum over the token's local rows (ascending expert id) of the
 // routing-weighted expert outputs (bf16 rows written by GEMM2), in fp32, then
-// cast once (ref_moe.py:166-167). Eight columns per thread.
+// cast once (ref_moe.py:166-167). Eight columns per thread. A direct-combine
+// call (direct_combine) has its fp32 sums in `tok_sum` already: they are cast
+// and cleared for the next call.
 __global__ void __launch_bounds__(256) finalize_kernel(const __nv_bfloat16* __restrict__ rows_buf,
                                                        const int32_t* __restrict__ token_rows,
                                                        void* __restrict__ out, int T, int out_fp32,
-                                                       const Plan* __restrict__ plan, int shared_e) {
+                                                       const Plan* __restrict__ plan, int shared_e,
+                                                       float* __restrict__ tok_sum) {
   griddep_wait();
+  const bool direct = direct_combine(plan->split2, T);
   // the shared expert's rows (one per token, in token order), added last
-  const int64_t shared_base = shared_e >= 0 ? (int64_t)plan->mtile_prefix[shared_e] * kTileM : -1;
+  const int64_t shared_base = (shared_e >= 0 && !direct) ? (int64_t)plan->mtile_prefix[shared_e] * kTileM : -1;
   constexpr int kC8 = kHidden / 8;  // 896 eight-column chunks per token
   const int64_t n = (int64_t)T * kC8;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const int t = static_cast<int>(i / kC8);
     const int c8 = static_cast<int>(i - (int64_t)t * kC8);
     float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
-    const int4* tr = reinterpret_cast<const int4*>(token_rows + (size_t)t * kTopK);
-    const int4 r0 = __ldg(tr), r1 = __ldg(tr + 1);
-    const int r[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+    if (direct) {
+      // tok_sum is [T][7168], i.e. eight-column chunk i at float4 2i, 2i+1
+      float4* g = reinterpret_cast<float4*>(tok_sum) + 2 * i;
+      s0 = __ldcg(g);
+      s1 = __ldcg(g + 1);
+      __stcg(g, make_float4(0.f, 0.f, 0.f, 0.f));
+      __stcg(g + 1, make_float4(0.f, 0.f, 0.f, 0.f));
+    } else {
+      const int4* tr = reinterpret_cast<const int4*>(token_rows + (size_t)t * kTopK);
+      const int4 r0 = __ldg(tr), r1 = __ldg(tr + 1);
+      const int r[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-      if (r[k] < 0) break;
-      // 8 bf16 columns of the row; bf16 -> f32 is exact (upper half of the word)
-      const uint4 q = __ldcs(reinterpret_cast<const uint4*>(rows_buf + (size_t)r[k] * kHidden) + c8);
-      s0.x += __uint_as_float(q.x << 16); s0.y += __uint_as_float(q.x & 0xFFFF0000u);
-      s0.z += __uint_as_float(q.y << 16); s0.w += __uint_as_float(q.y & 0xFFFF0000u);
-      s1.x += __uint_as_float(q.z << 16); s1.y += __uint_as_float(q.z & 0xFFFF0000u);
-      s1.z += __uint_as_float(q.w << 16); s1.w += __uint_as_float(q.w & 0xFFFF0000u);
-    }
-    if (shared_base >= 0) {
-      const uint4 q = __ldcs(reinterpret_cast<const uint4*>(rows_buf + (size_t)(shared_base + t) * kHidden) + c8);
-      s0.x += __uint_as_float(q.x << 16); s0.y += __uint_as_float(q.x & 0xFFFF0000u);
-      s0.z += __uint_as_float(q.y << 16); s0.w += __uint_as_float(q.y & 0xFFFF0000u);
-      s1.x += __uint_as_float(q.z << 16); s1.y += __uint_as_float(q.z & 0xFFFF0000u);
-      s1.z += __uint_as_float(q.w << 16); s1.w += __uint_as_float(q.w & 0xFFFF0000u);
+      for (int k = 0; k < kTopK; ++k) {
+        if (r[k] < 0) break;
+        // 8 bf16 columns of the row; bf16 -> f32 is exact (upper half of the word)
+        const uint4 q = __ldcs(reinterpret_cast<const uint4*>(rows_buf + (size_t)r[k] * kHidden) + c8);
+        s0.x += __uint_as_float(q.x << 16); s0.y += __uint_as_float(q.x & 0xFFFF0000u);
+        s0.z += __uint_as_float(q.y << 16); s0.w += __uint_as_float(q.y & 0xFFFF0000u);
+        s1.x += __uint_as_float(q.z << 16); s1.y += __uint_as_float(q.z & 0xFFFF0000u);
+        s1.z += __uint_as_float(q.w << 16); s1.w += __uint_as_float(q.w & 0xFFFF0000u);
+      }
+      if (shared_base >= 0) {
+        const uint4 q = __ldcs(reinterpret_cast<const uint4*>(rows_buf + (size_t)(shared_base + t) * kHidden) + c8);
+        s0.x += __uint_as_float(q.x << 16); s0.y += __uint_as_float(q.x & 0xFFFF0000u);
+        s0.z += __uint_as_float(q.y << 16); s0.w += __uint_as_float(q.y & 0xFFFF0000u);
+        s1.x += __uint_as_float(q.z << 16); s1.y += __uint_as_float(q.z & 0xFFFF0000u);
+        s1.z += __uint_as_float(q.w << 16); s1.w += __uint_as_float(q.w & 0xFFFF0000u);
+      }
     }
     if (out_fp32) {
       float4* o = reinterpret_cast<float4*>(out) + 2 * i;
@@ -468,7 +492,7 @@ cudaError_t launch_finalize(const Workspace& ws, int T, void* out, int out_fp32,
   if (blocks > 16 * kSMs) blocks = 16 * kSMs;
   return launch_k(finalize_kernel, dim3((unsigned)blocks), dim3(256), 0, s, true,
                   static_cast<const __nv_bfloat16*>(ws.out_rows), static_cast<const int32_t*>(ws.token_rows), out, T,
-                  out_fp32, static_cast<const Plan*>(ws.plan), shared_e);
+                  out_fp32, static_cast<const Plan*>(ws.plan), shared_e, ws.g2_part);
 }
 
 }  // namespace moe
