@@ -287,6 +287,35 @@ def _roofline_gemm1(stats, g1_ms, hbm_peak, peak_src, fp8, fp8_2x_sustained, tra
             "algorithmic_bytes_per_launch": int(byts / max(1, len(stats)))}
 
 
+def _packed_inputs(acts_cpu, dev):
+    """One pinned host buffer holding a call's inputs (logits | bias | hidden |
+    hidden_scale, each at a 16-byte-aligned offset) and a device buffer of the
+    same layout with the layer's input tensors as views into it, so that the
+    end-to-end step moves its inputs with one host-to-device copy."""
+    import torch
+
+    wl = importlib.import_module("flashinfer-mlsys_b200.workloads")
+    T = acts_cpu.T
+    parts = [t.contiguous().reshape(-1).view(torch.uint8)
+             for t in (acts_cpu.logits, acts_cpu.bias, acts_cpu.hidden, acts_cpu.hidden_scale)]
+    offs, n = [], 0
+    for t in parts:
+        offs.append(n)
+        n += (t.numel() + 15) // 16 * 16
+    host = torch.empty(n, dtype=torch.uint8).pin_memory()
+    for o, t in zip(offs, parts):
+        host[o:o + t.numel()].copy_(t)
+    buf = torch.empty(n, dtype=torch.uint8, device=dev)
+
+    def view(i, dtype, shape):
+        nbytes = parts[i].numel()
+        return buf[offs[i]:offs[i] + nbytes].view(dtype).view(shape)
+
+    acts = wl.Activations(view(0, torch.float32, (T, 256)), view(1, torch.bfloat16, (256,)),
+                          view(2, torch.float8_e4m3fn, (T, 7168)), view(3, torch.float32, (56, T)))
+    return host, buf, acts
+
+
 def _measure_layer(pkg, lib, dev, stream, flush, w, acts_cpu, e_local, steps, warmup, kernels=True, e2e=True):
     """Per-T device time, per-kernel times, host enqueue and end-to-end time of
     the layer (one library call per T per step) on weights `w`."""
@@ -357,31 +386,31 @@ def _measure_layer(pkg, lib, dev, stream, flush, w, acts_cpu, e_local, steps, wa
             torch.cuda.synchronize()
         res["host_us"] = host
     if e2e:
-        # end to end through the public API with host buffers (pinned): H2D of
-        # the call's inputs and D2H of its output inside the events
-        host_in = {T: [acts_cpu[T].logits.pin_memory(), acts_cpu[T].bias.pin_memory(),
-                       acts_cpu[T].hidden.view(torch.uint8).pin_memory(), acts_cpu[T].hidden_scale.pin_memory()]
-                   for T in Ts}
+        # end to end through the public API with host buffers (pinned): the
+        # H2D copy of the call's inputs (one packed buffer) and the D2H of its
+        # output inside the events
+        packed = {T: _packed_inputs(acts_cpu[T], dev) for T in Ts}
         host_out = {T: torch.empty((T, 7168), dtype=torch.bfloat16).pin_memory() for T in Ts}
         e2e_ev = {T: [] for T in Ts}
         for i in range(warmup + steps):
             for T in Ts:
-                a = acts[T]
+                host_in, dev_in, a = packed[T]
                 flush.zero_()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-                a.logits.copy_(host_in[T][0], non_blocking=True)
-                a.bias.copy_(host_in[T][1], non_blocking=True)
-                a.hidden.view(torch.uint8).copy_(host_in[T][2], non_blocking=True)
-                a.hidden_scale.copy_(host_in[T][3], non_blocking=True)
-                call(T)
+                dev_in.copy_(host_in, non_blocking=True)
+                pkg.kernel(a.logits, a.bias, a.hidden, a.hidden_scale, w.w13, w.s13, w.w2, w.s2, w.offset, 2.5,
+                           outs[T])
                 host_out[T].copy_(outs[T], non_blocking=True)
                 e1.record(stream)
                 if i >= warmup:
                     e2e_ev[T].append((e0, e1))
         torch.cuda.synchronize()
+        for T in Ts:  # the packed inputs reached the device intact
+            if not torch.equal(packed[T][1].cpu(), packed[T][0]):
+                raise RuntimeError("packed input copy mismatch")
         res["e2e_ms"] = {T: statistics.mean(a.elapsed_time(b) for a, b in e2e_ev[T]) for T in Ts}
-        res["h2d"] = {T: int(sum(x.numel() * x.element_size() for x in host_in[T])) for T in Ts}
+        res["h2d"] = {T: int(packed[T][0].numel()) for T in Ts}
         res["d2h"] = {T: T * 7168 * 2 for T in Ts}
     return res
 
@@ -577,20 +606,17 @@ def bench_ep(args, rank, world, local, dev):
             ph += np.array([marks[i].elapsed_time(marks[i + 1]) for i in range(nph)])
         ph_t = torch.tensor(ph / args.steps, device=dev)
         dist.all_reduce(ph_t, op=dist.ReduceOp.MAX)
-        # end to end: H2D of this rank's inputs, the call, D2H of the output
-        host = [acts.logits.pin_memory(), acts.bias.pin_memory(), acts.hidden.view(torch.uint8).pin_memory(),
-                acts.hidden_scale.pin_memory()]
+        # end to end: H2D of this rank's inputs (one packed buffer), the call,
+        # D2H of the output
+        host_in, dev_in, a_e2e = _packed_inputs(acts, dev)
         host_out = torch.empty((T, 7168), dtype=torch.bfloat16).pin_memory()
         e2e = []
         for i in range(args.warmup + args.steps):
             flush.zero_()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            a.logits.copy_(host[0], non_blocking=True)
-            a.bias.copy_(host[1], non_blocking=True)
-            a.hidden.view(torch.uint8).copy_(host[2], non_blocking=True)
-            a.hidden_scale.copy_(host[3], non_blocking=True)
-            o = call(a)
+            dev_in.copy_(host_in, non_blocking=True)
+            o = call(a_e2e)
             host_out.copy_(o, non_blocking=True)
             e1.record(stream)
             if i >= args.warmup:
@@ -638,7 +664,7 @@ def bench_ep(args, rank, world, local, dev):
                                                                                * 1e-6) / 1e9, 1),
                          "traffic": None},
             "e2e": {"value": round(float(e2e_t.item()) * 1e3, 2), "unit": "us/call",
-                    "h2d_bytes_per_step": int(sum(x.numel() * x.element_size() for x in host)),
+                    "h2d_bytes_per_step": int(host_in.numel()),
                     "d2h_bytes_per_step": T * 7168 * 2},
             "gpu_launches": 8 * args.steps, "clocks": clk.summary(),
         })
