@@ -98,6 +98,29 @@ def test_parity_skewed_prefill_every_mtile(gpu_available, T):
     check_output(out, ref["out_f32"], rows=rows)
 
 
+@pytest.mark.parametrize("T", [64, 100, 256])
+def test_parity_one_local_expert_direct_combine(gpu_available, T):
+    """Every token's only local expert is expert 3 (bias +16 on it, -8 on the
+    other 31 local experts), so the call has one or two m-tiles: both GEMMs
+    are split along K, and GEMM2 adds into per-token fp32 sums (the direct
+    combine) with a full 64-row skinny tile (T=64, hi and lo in one MMA) and
+    with 128-row tiles (T=100, 256). Routing, counts and every output row."""
+    wl = workloads()
+    a = wl.make_activations(T, seed=4242 + T)
+    bias = a.bias.float()
+    bias[:32] = -8.0
+    bias[3] = 16.0
+    acts = wl.Activations(a.logits, bias.to(torch.bfloat16), a.hidden, a.hidden_scale)
+    w = gpu_weights()
+    out, ids, wts, cnt = run_gpu(acts.to(DEV), w)
+    counts = cnt.cpu().numpy()
+    assert int(counts[3]) == T and int(counts.sum()) == T
+    ref = oracle_run(acts, w)
+    check_routing(ref["routing"], ids, cnt, 0, 32)
+    check_weights(ref["routing"], ids, wts)
+    check_output(out, ref["out_f32"])
+
+
 def test_parity_beyond_benchmark_sizes_T65536(gpu_available):
     """Four times the largest benchmark call (near-uniform routing, ~16k
     local rows, a 13.5 GB workspace): 64-bit indexing of rows, scales and
