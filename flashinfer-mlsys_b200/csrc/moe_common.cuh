@@ -52,23 +52,26 @@ constexpr int kInterCols = 2 * kInter;        // 4096 bytes per intermediate row
 
 constexpr int kStageA = kTileM * kBlk;        // 16 KB of e4m3 (one 128-row A tile)
 constexpr int kStageB = kTileN * kBlk;        // 32 KB of e4m3
-// kSkinny: calls with at most 64 tokens load 64-row token tiles (8 KB), which
-// leaves room for one more stage of weights in flight. The MMA still reads
-// 128 rows; rows 64-127 then see unrelated shared memory and only produce
-// accumulator rows that are never stored (every m-tile has <= 64 valid rows).
+// kSkinny = 1: calls with at most 64 tokens load 64-row token tiles (8 KB),
+// which leaves room for one more stage of weights in flight. kSkinny = 2
+// (GEMM1 of calls with at most kTinyMaxRows tokens): 16-row token tiles
+// (2 KB) and six stages of weights in flight. The MMA still reads 128 rows;
+// the rows past the tile then see unrelated shared memory (inside the ring)
+// and only produce accumulator rows that are never stored.
+constexpr int kTinyMaxRows = 16;
 template <int kMode, int kSkinny = 0>
 struct GemmCfg {
   static constexpr int kATiles = (kMode == 1) ? 1 : 2;          // GEMM2: hi and lo
-  static constexpr int kARows = kSkinny ? 64 : kTileM;
+  static constexpr int kARows = kSkinny == 2 ? kTinyMaxRows : (kSkinny ? 64 : kTileM);
   static constexpr int kABytes = kARows * kBlk;                 // bytes loaded (and slot size) per A tile
   static constexpr int kStageBytes = kATiles * kABytes + kStageB;
-  static constexpr int kStages = kSkinny ? ((kMode == 1) ? 5 : 4) : ((kMode == 1) ? 4 : 3);
+  static constexpr int kStages = kSkinny == 2 ? 6 : (kSkinny ? ((kMode == 1) ? 5 : 4) : ((kMode == 1) ? 4 : 3));
   static constexpr int kRing = kStages * kStageBytes;
   static constexpr int kNKB = (kMode == 1) ? kKB1 : kKB2;
   static constexpr int kNT = (kMode == 1) ? kNT1 : kNT2;
 };
-constexpr int kMaxStages = 5;
-constexpr int kRingBytes = 200 * 1024;          // >= kRing of every configuration
+constexpr int kMaxStages = 6;
+constexpr int kRingBytes = 204 * 1024;          // >= kRing of every configuration
 constexpr int kSkinnyMaxRows = 64;
 constexpr int kDecMaxT = 64;                   // largest call served by the fused decode kernel
 

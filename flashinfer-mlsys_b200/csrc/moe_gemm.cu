@@ -315,6 +315,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const __grid_constant__ CUtensorMap map_ws, GemmArgs p) {
   using Cfg = GemmCfg<kMode, kSkinny>;
   static_assert(Cfg::kRing <= kRingBytes && Cfg::kStages <= kMaxStages, "stage ring does not fit");
+  static_assert((Cfg::kATiles * Cfg::kABytes) % 1024 == 0 && Cfg::kStageBytes % 1024 == 0,
+                "128-byte-swizzled tiles need 1024-byte alignment");
   constexpr int NT = Cfg::kNT;
   constexpr int kStages = Cfg::kStages;
   constexpr int kStageBytes = Cfg::kStageBytes;
@@ -404,7 +406,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int units = total_mtiles * NT * split;
   const uint32_t tmem = ctl->tmem_base;
 
-  constexpr bool kGather = (kMode == 1 && kSkinny == 1);
+  constexpr bool kGather = (kMode == 1 && kSkinny >= 1);
   if (warp == 0 && kGather) {
     // ============ TMA producer, rows gathered from hidden_states ============
     // lane 0 waits for a free stage and loads the weights; lane l gathers
@@ -787,6 +789,14 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
 
 }  // namespace
 
+// GEMM1 of calls with at most this many tokens uses 16-row token tiles and
+// six weight stages (a shared expert adds no rows beyond T).
+#ifndef MOE_TINY_MAX_T
+#define MOE_TINY_MAX_T 16
+#endif
+constexpr int kTinyMaxT = MOE_TINY_MAX_T;
+static_assert(kTinyMaxT <= kTinyMaxRows, "tiny GEMM1 tiles hold kTinyMaxRows rows");
+
 // GEMM1 directly follows the routing kernel that writes the plan, so it reads
 // the plan after its programmatic-launch wait. GEMM2 was released by GEMM1
 // after that wait: the plan is complete when GEMM2 starts, and GEMM2 loads it
@@ -794,6 +804,8 @@ cudaError_t launch_gemm(const Workspace& ws, const CUtensorMap& map_a, const CUt
 cudaError_t launch_gemm1(const Workspace& ws, const CUtensorMap& map_a, const CUtensorMap& map_w,
                          const float* w_scale, cudaStream_t s, bool skinny, const float* x_scale, int64_t T,
                          const CUtensorMap& map_ws, const float* ws_scale, int shared_e) {
+  if (skinny && T <= kTinyMaxT)
+    return launch_gemm<1, 2>(ws, map_a, map_w, w_scale, s, 0, map_ws, ws_scale, shared_e, x_scale, T);
   return skinny ? launch_gemm<1, 1>(ws, map_a, map_w, w_scale, s, 0, map_ws, ws_scale, shared_e, x_scale, T)
                 : launch_gemm<1, 0>(ws, map_a, map_w, w_scale, s, 0, map_ws, ws_scale, shared_e);
 }
