@@ -16,9 +16,11 @@
 //     with 64-row tiles their hi and lo tiles form one 128-row operand: one
 //     MMA per K slice puts hi x W in TMEM lanes 0-63 and lo x W in 64-127.
 //
-// Warp roles (576 threads, one CTA per SM):
+// Warp roles (608 threads, one CTA per SM):
 //   warp 0      TMA producer (one elected lane): A tile 128x128 + two B slabs
-//               128x128 per K block into a 4-stage shared-memory ring.
+//               128x128 per K block into a shared-memory ring of 3-6 stages
+//               (GemmCfg); GEMM1 of calls with at most 64 tokens gathers its
+//               A rows from hidden_states with all 32 lanes (tile::gather4).
 //   warp 1      TMEM owner + MMA issuer (one lane): 4 x tcgen05.mma
 //               (M128 N256 K32, e4m3 x e4m3 -> f32) per K block into one of
 //               two 256-column TMEM partial accumulators.
