@@ -40,3 +40,26 @@ def test_reference_and_our_arm_share_the_config_keys():
         assert c["parallelism"] == f"ep{world}"
     for name in bench.SWEEP:
         assert bench._config(name, 1, bench.WORKLOADS[name][0])["T"] == list(bench.WORKLOADS[name][0])
+
+
+@pytest.mark.parametrize("T", [1, 7, 64, 300])
+def test_packed_end_to_end_inputs(monkeypatch, T):
+    """The end-to-end step moves a call's inputs with one copy of a packed
+    buffer: every input tensor is a contiguous view of it at a 16-byte-aligned
+    offset, with its source's dtype, shape and bytes (checked here with a
+    CPU 'device' buffer; page-locking needs a GPU)."""
+    import torch
+
+    sys.path.insert(0, ROOT)
+    import bench
+    from conftest import workloads
+
+    monkeypatch.setattr(torch.Tensor, "pin_memory", lambda self: self)
+    a = workloads().make_activations(T, seed=T)
+    host, buf, v = bench._packed_inputs(a, "cpu")
+    assert host.dtype == torch.uint8 and host.numel() == buf.numel()
+    buf.copy_(host)
+    for got, ref in ((v.logits, a.logits), (v.bias, a.bias), (v.hidden, a.hidden), (v.hidden_scale, a.hidden_scale)):
+        assert got.dtype == ref.dtype and tuple(got.shape) == tuple(ref.shape) and got.is_contiguous()
+        assert (got.data_ptr() - buf.data_ptr()) % 16 == 0
+        assert torch.equal(got.reshape(-1).view(torch.uint8), ref.reshape(-1).view(torch.uint8))
