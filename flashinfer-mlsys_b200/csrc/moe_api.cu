@@ -227,7 +227,7 @@ inline void prof_mark(int i, cudaStream_t s) {
 }
 
 // Calls with 1..kDecMaxT tokens can be served by the fused decode kernel.
-// It is off by default (the five-kernel pipeline measured faster on the
+// It is off by default (the four-kernel pipeline measured faster on the
 // decode sweep); MOE_FP8_DS_FUSED_DECODE=1 in the environment or
 // moe_fp8_ds_set_fused_decode(1) turns it on.
 int g_fused_decode = -1;

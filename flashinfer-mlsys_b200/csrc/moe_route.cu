@@ -1,6 +1,8 @@
-// moe_route.cu — K1 (DeepSeek-V3 no-aux routing + local histogram + plan),
-// K1b (token permutation into the expert-major padded layout) and K4
-// (fp32 combine accumulator -> bf16/fp32 output).
+// moe_route.cu — K1 (DeepSeek-V3 no-aux routing + local histogram + plan,
+// fused with the token permutation into the expert-major padded layout in one
+// cooperative launch; a routing-only variant for the routing entry points)
+// and K4 (the per-token combine of GEMM2's rows, or the cast of the per-token
+// fp32 sums of a direct-combine call, to bf16/fp32 output).
 //
 // Routing semantics follow reference moe/ref_moe.py:95-126:
 //   s = 1 / (1 + exp(-logit)); sb = s + bias
